@@ -1,0 +1,399 @@
+"""Benchmark of the B200 gpt-oss MoE layer (one JSON line on rank 0).
+
+Default workload: the gpt-oss-120b-shaped MoE layer (H = I = 2880, 128 experts,
+top-4, MXFP4 experts) over an 8192-token prefill batch, all experts resident
+on each GPU at N=1.  A "step" is one layer forward: router, dispatch, gate_up +
+SwiGLU, down, weighted combine.  Inputs are seeded synthetic tensors (no
+checkpoint exists offline); the weights (1.69 GB) are larger than L2, so no
+extra L2 flush is needed between steps.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload gptoss120b-prefill-8192|gptoss120b-decode-T|gptoss20b-prefill-4096]
+
+``--impl reference`` times the reference's CPU path restated in ``oracle``
+(bf16 per-expert loop, the CPU baseline) on a bounded sample on rank 0.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+from blockstreamer_b200 import kernels  # noqa: E402
+from blockstreamer_b200.synthetic import (CASES, algorithmic_bytes, algorithmic_flops,  # noqa: E402
+                                          expert_bytes, make_layer, make_tokens)
+
+METRIC = "MoE-layer tokens/s at gpt-oss-120b shape"
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+FP4_DENSE_NOMINAL_TFLOPS = 9000.0
+
+
+def parse_workload(name: str):
+    if name.startswith("gptoss120b-prefill-"):
+        return "gptoss120b", 4, int(name.rsplit("-", 1)[1])
+    if name.startswith("gptoss120b-decode-"):
+        return "gptoss120b", 3, int(name.rsplit("-", 1)[1])
+    if name.startswith("gptoss20b-prefill-"):
+        return "gptoss20b", 2, int(name.rsplit("-", 1)[1])
+    raise SystemExit(f"unknown workload {name}")
+
+
+def load_peaks():
+    p = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return d, "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            f = [c.strip() for c in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_setup(n_gpus: int):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------- reference arm
+
+def cpu_inputs(key: str, case_id: int, T: int):
+    shape = CASES[key]
+    return shape, make_layer(shape, case_id), make_tokens(T, shape.hidden, case_id)
+
+
+def cpu_sample(shape, p, x, experts_in_sample: int = 1):
+    """Time the reference's CPU path (oracle port) on a bounded sample of the
+    workload: the router over all T tokens plus the full expert work of
+    ``experts_in_sample`` experts; the expert time is scaled to all hit experts."""
+    from oracle import moe as omoe
+    T = x.shape[0]
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    pe = {k.split(".", 1)[1]: v for k, v in p.items() if k.startswith("experts.")}
+    t0 = time.perf_counter()
+    _, sc, idx = omoe.router(x.float(), p["router.weight"], p["router.bias"], shape.top_k)
+    t_router = time.perf_counter() - t0
+    hit = sorted(set(idx.reshape(-1).tolist()))
+    subset = hit[:experts_in_sample]
+    t0 = time.perf_counter()
+    omoe.experts_port(x, idx, sc, pe, experts_subset=subset)
+    t_exp = time.perf_counter() - t0
+    t_total = t_router + t_exp * len(hit) / max(len(subset), 1)
+    return {"value": T / t_total, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": (f"router over all {T} tokens ({t_router:.2f} s) + the full bf16 expert loop "
+                       f"of {len(subset)} of {len(hit)} hit experts ({t_exp:.2f} s), expert time "
+                       f"scaled x{len(hit) / max(len(subset), 1):.0f}"),
+            "seconds": t_router + t_exp}
+
+
+def run_reference(args, rank, world):
+    key, case_id, T = parse_workload(args.workload)
+    if rank != 0:
+        return
+    vals = []
+    cb = None
+    shape, p, x = cpu_inputs(key, case_id, T)
+    for i in range(args.warmup + args.steps):
+        r = cpu_sample(shape, p, x, experts_in_sample=1)
+        if i >= args.warmup:
+            vals.append(r["value"])
+            cb = r
+    v = statistics.median(vals)
+    cb["value"] = v
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * T / v,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic", "config": {"workload": args.workload},
+            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- our arm
+
+STAGES = ("router", "dispatch", "gate_up", "down", "combine")
+LAUNCHES = {"router": 1, "dispatch": 4, "gate_up": 1, "down": 1, "combine": 1}
+
+
+def layer_stages(x, p, k, algo, bufs):
+    """The layer as its C-ABI stages (the same kernels bs_moe_forward runs)."""
+    E = p["experts.gate_up_proj_blocks"].shape[0]
+    T = x.shape[0]
+
+    def router():
+        _, bufs["sc"], bufs["idx"] = kernels.router(x, p["router.weight"], p["router.bias"], k,
+                                                    index_dtype=torch.int32, return_logits=T <= 8)
+
+    def dispatch():
+        bufs["d"] = kernels.dispatch(bufs["idx"], E, x)
+
+    def gate_up():
+        d = bufs["d"]
+        bufs["h"] = kernels.moe_gate_up(d.x_perm, d.expert_offsets, p["experts.gate_up_proj_blocks"],
+                                        p["experts.gate_up_proj_scales"], p["experts.gate_up_proj_bias"],
+                                        algo=algo)
+
+    def down():
+        d = bufs["d"]
+        bufs["y"] = kernels.moe_down(bufs["h"], d.expert_offsets, p["experts.down_proj_blocks"],
+                                     p["experts.down_proj_scales"], p["experts.down_proj_bias"], algo=algo)
+
+    def combine():
+        bufs["out"] = kernels.combine(bufs["y"], bufs["d"].row_of_slot, bufs["sc"], T)
+
+    return {"router": router, "dispatch": dispatch, "gate_up": gate_up, "down": down, "combine": combine}
+
+
+def run_ours(args, rank, world, local):
+    key, case_id, T_total = parse_workload(args.workload)
+    shape = CASES[key]
+    dev = torch.device("cuda", torch.cuda.current_device())
+    if world > 1:
+        from blockstreamer_b200.expert_parallel import run_bench_ep
+        return run_bench_ep(args, rank, world, local, shape, case_id, T_total)
+    T = T_total
+    k = shape.top_k
+    algo = {"auto": kernels.ALGO_AUTO, "gemv": kernels.ALGO_GEMV, "tcgen05": kernels.ALGO_TCGEN05}[args.algo]
+    p = make_layer(shape, case_id, device=dev)
+    x = make_tokens(T, shape.hidden, case_id, device=dev)
+    E = shape.experts
+    gu = (p["experts.gate_up_proj_blocks"], p["experts.gate_up_proj_scales"], p["experts.gate_up_proj_bias"])
+    dn = (p["experts.down_proj_blocks"], p["experts.down_proj_scales"], p["experts.down_proj_bias"])
+    ws = torch.empty(kernels._lib.load().bs_moe_workspace_bytes(T, shape.hidden, shape.intermediate, E, k),
+                     dtype=torch.uint8, device=dev)
+
+    def step():
+        return kernels.moe_forward(x, *gu, *dn, k, router_weight=p["router.weight"],
+                                   router_bias=p["router.bias"], algo=algo, workspace=ws)
+
+    for _ in range(args.warmup):
+        out, sc, idx = step()
+    torch.cuda.synchronize()
+    distinct = int(torch.unique(idx).numel())
+    counts = torch.bincount(idx.reshape(-1).long(), minlength=E)
+    assert kernels.device_status(clear=True) == 0
+
+    # --- value: K back-to-back layer forwards, device-timed
+    st = torch.cuda.current_stream()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier(world)
+        torch.cuda.synchronize()
+        ev0.record(st)
+        for _ in range(args.steps):
+            step()
+        ev1.record(st)
+        torch.cuda.synchronize()
+        barrier(world)
+    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world)
+    value = T / (ms * 1e-3)
+
+    # --- per-stage breakdown over K more steps (same kernels, events between stages)
+    bufs = {}
+    stages = layer_stages(x, p, k, algo, bufs)
+    for fn in stages.values():
+        fn()
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(len(STAGES) + 1)] for _ in range(args.steps)]
+    for i in range(args.steps):
+        evs[i][0].record(st)
+        for j, name in enumerate(STAGES):
+            stages[name]()
+            evs[i][j + 1].record(st)
+    torch.cuda.synchronize()
+    stage_ms = {n: statistics.mean(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(args.steps))
+                for j, n in enumerate(STAGES)}
+
+    # --- e2e through the public API with host buffers
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty_like(x_host).pin_memory()
+    x_dev = torch.empty_like(x)
+    e2e_ms = []
+    for i in range(args.warmup + args.steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        x_dev.copy_(x_host, non_blocking=True)
+        o, _, _ = kernels.moe_forward(x_dev, *gu, *dn, k, router_weight=p["router.weight"],
+                                      router_bias=p["router.bias"], algo=algo, workspace=ws)
+        out_host.copy_(o, non_blocking=True)
+        b.record(st)
+        b.synchronize()
+        if i >= args.warmup:
+            e2e_ms.append(a.elapsed_time(b))
+    e2e_ms_v = max_over_ranks(statistics.mean(e2e_ms), world)
+
+    # --- roofline of the dominant kernel
+    peaks, peak_src = load_peaks()
+    flops_pair = 6.0 * shape.hidden * shape.intermediate
+    S = T * k
+    stage_flops = {"gate_up": S * 4.0 * shape.hidden * shape.intermediate,
+                   "down": S * 2.0 * shape.hidden * shape.intermediate,
+                   "router": 2.0 * T * shape.hidden * E}
+    G = shape.hidden // 32
+    gu_bytes = distinct * (2 * shape.intermediate * G * 17 + 2 * shape.intermediate * 2) + S * shape.hidden * 2 + S * shape.intermediate * 2
+    dn_bytes = distinct * (shape.hidden * (shape.intermediate // 32) * 17 + shape.hidden * 2) + S * shape.intermediate * 2 + S * shape.hidden * 2
+    stage_bytes = {"gate_up": gu_bytes, "down": dn_bytes,
+                   "router": E * shape.hidden * 4 + T * shape.hidden * 2,
+                   "dispatch": 2 * S * shape.hidden * 2, "combine": S * shape.hidden * 2 + T * shape.hidden * 2}
+    dom = max(stage_ms, key=stage_ms.get)
+    tensor_bound = (S / max(distinct, 1)) > 64 and dom in ("gate_up", "down")
+    dur_s = stage_ms[dom] * 1e-3
+    if tensor_bound:
+        achieved = stage_flops[dom] / dur_s / 1e12
+        peak = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
+        roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak, "traffic": None, "kernel": dom,
+                "peak_source": f"{peak_src} bf16 dense sustained (cuBLAS) — the MMA runs bf16 x bf16"}
+    else:
+        achieved = stage_bytes[dom] / dur_s / 1e9
+        peak = peaks["hbm_gbs"]
+        roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "traffic": None, "kernel": dom,
+                "peak_source": f"{peak_src} HBM copy bandwidth"}
+    roof["algorithmic"] = {"flops": stage_flops.get(dom), "bytes": stage_bytes.get(dom),
+                           "launch_ms": stage_ms[dom]}
+    layer_flops = algorithmic_flops(T, shape)
+    layer_bytes = algorithmic_bytes(T, shape, distinct)
+    t_fp4 = layer_flops / (FP4_DENSE_NOMINAL_TFLOPS * 1e12)
+    t_hbm = layer_bytes / (peaks["hbm_gbs"] * 1e9)
+    layer_roof = {"flops": layer_flops, "bytes": layer_bytes, "distinct_experts": distinct,
+                  "floor_us_fp4_nominal": t_fp4 * 1e6, "floor_us_hbm_measured": t_hbm * 1e6,
+                  "frac_of_fp4_hbm_roofline": max(t_fp4, t_hbm) / (ms * 1e-3),
+                  "frac_of_bf16_measured": (layer_flops / (ms * 1e-3) / 1e12) / peaks["bf16_tflops"],
+                  "stage_ms": stage_ms}
+
+    clocks = clk.summary()
+    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": args.workload, "tokens": T, "hidden": shape.hidden,
+                       "intermediate": shape.intermediate, "experts": E, "top_k": k,
+                       "weights": "MXFP4 e2m1 + e8m0 scales (uniform codes, scales U{%d..%d})" % (shape.scale_lo, shape.scale_hi),
+                       "algo": args.algo, "l2": "inputs larger than L2 (1.69 GB of expert weights per step)",
+                       "expert_rows_min_max": [int(counts.min()), int(counts.max())]},
+            "roofline": roof, "layer_roofline": layer_roof,
+            "e2e": {"value": T / (e2e_ms_v * 1e-3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": x.numel() * 2,
+                    "api": "blockstreamer_b200.kernels.moe_forward -> bs_moe_forward"},
+            "clocks": clocks, "gpu_launches": sum(LAUNCHES.values()) * args.steps}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        shape_c, p_c, x_c = cpu_inputs(key, case_id, T)
+        cb = cpu_sample(shape_c, p_c, x_c, experts_in_sample=1)
+        line["cpu_baseline"] = {k2: cb[k2] for k2 in ("value", "unit", "cores", "kind", "sample")}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="gptoss120b-prefill-8192")
+    ap.add_argument("--algo", choices=["auto", "gemv", "tcgen05"], default="auto")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        return run_reference(args, rank, world)
+    rank, world, local = dist_setup(args.gpus)
+    try:
+        run_ours(args, rank, world, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

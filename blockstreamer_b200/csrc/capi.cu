@@ -1,0 +1,197 @@
+// C-ABI entry points that compose the kernels: expert projections (GEMV or
+// tcgen05 grouped GEMM), mxfp4_matmul, and the whole-layer forward.
+#include "bs_common.cuh"
+
+namespace bs {
+
+int router_launch(const void* x, int x_dtype, const void* weight, const void* bias, int w_dtype,
+                  int64_t T, int64_t H, int64_t E, int64_t k, float* logits, float* scores,
+                  void* indices, int index_dtype, cudaStream_t st);
+size_t dispatch_workspace_bytes(int64_t T, int64_t k, int64_t E);
+int dispatch_launch(const void* indices, int index_dtype, int64_t T, int64_t k, int64_t E,
+                    const void* x, int64_t H, int32_t* offsets, int32_t* row_of_slot,
+                    int32_t* token_of_row, void* x_perm, void* ws, size_t ws_bytes,
+                    cudaStream_t st);
+int combine_launch(const void* y, const int32_t* row_of_slot, const float* weights, int64_t T,
+                   int64_t k, int64_t H, void* out, cudaStream_t st);
+int gemv_gate_up_launch(const void* x, const int32_t* offsets, int64_t rows_total, int64_t E,
+                        int64_t H, int64_t I, const void* blocks, const void* scales,
+                        const void* bias, int bias_f32, float alpha, float limit, void* h,
+                        cudaStream_t st);
+int gemv_plain_launch(const void* x, const int32_t* offsets, int64_t rows_total, int64_t E,
+                      int64_t K, int64_t N, const void* blocks, const void* scales,
+                      const void* bias, int bias_f32, void* y, cudaStream_t st);
+// tcgen05 grouped GEMM (grouped_gemm.cu).  mode 0: gate_up + SwiGLU, 1: plain + bias.
+int tc_grouped_launch(int mode, const void* x, const int32_t* offsets, int64_t rows_total,
+                      int64_t max_rows_per_expert, int64_t E, int64_t K, int64_t N,
+                      const void* blocks, const void* scales, const void* bias, int bias_f32,
+                      float alpha, float limit, void* out, cudaStream_t st);
+
+namespace {
+
+// Tokens per expert above which the tensor-core path wins over the GEMV.
+constexpr int64_t kGemvMaxRowsPerExpert = 16;
+
+int pick_algo(int algo, int64_t rows_total, int64_t E) {
+  if (algo != BS_ALGO_AUTO) return algo;
+  return (rows_total <= kGemvMaxRowsPerExpert * E) ? BS_ALGO_GEMV : BS_ALGO_TCGEN05;
+}
+
+int check_expert_args(const char* fn, const void* x, const void* blocks, const void* scales,
+                      const void* out, int64_t rows_total, int64_t E, int64_t K, int64_t N,
+                      int bias_dtype, int algo) {
+  BS_ARG(x && blocks && scales && out, "%s: null pointer", fn);
+  BS_ARG(rows_total >= 0 && E > 0 && K > 0 && N > 0, "%s: bad sizes", fn);
+  BS_ARG(K % 32 == 0, "%s: contraction size %lld is not a multiple of 32", fn, (long long)K);
+  BS_ARG(E <= 1024, "%s: at most 1024 experts", fn);
+  BS_ARG(rows_total < (int64_t)INT32_MAX && N < (int64_t)INT32_MAX, "%s: sizes too large", fn);
+  BS_ARG(bias_dtype == BS_BF16 || bias_dtype == BS_F32, "%s: bias dtype must be bf16 or f32", fn);
+  BS_ARG(algo >= BS_ALGO_AUTO && algo <= BS_ALGO_TCGEN05, "%s: unknown algo %d", fn, algo);
+  BS_ALIGNED16(x, "x");
+  BS_ALIGNED16(blocks, "blocks");
+  return BS_OK;
+}
+
+}  // namespace
+
+int gate_up(const void* x, const int32_t* offsets, int64_t rows_total, int64_t max_rows, int64_t E,
+            int64_t H, int64_t I, const void* blocks, const void* scales, const void* bias,
+            int bias_dtype, float alpha, float limit, void* h, int algo, cudaStream_t st) {
+  BS_TRY(check_expert_args("bs_moe_gate_up", x, blocks, scales, h, rows_total, E, H, 2 * I,
+                           bias_dtype, algo));
+  BS_ARG(offsets, "bs_moe_gate_up: null expert_offsets");
+  BS_ARG(I % 8 == 0, "bs_moe_gate_up: intermediate size must be a multiple of 8");
+  if (rows_total == 0) return BS_OK;
+  BS_TRY(check_device());
+  const int a = pick_algo(algo, rows_total, E);
+  const int bf32 = bias_dtype == BS_F32;
+  if (a == BS_ALGO_GEMV)
+    return gemv_gate_up_launch(x, offsets, rows_total, E, H, I, blocks, scales, bias, bf32, alpha,
+                               limit, h, st);
+  return tc_grouped_launch(0, x, offsets, rows_total, max_rows, E, H, 2 * I, blocks, scales, bias,
+                           bf32, alpha, limit, h, st);
+}
+
+int down(const void* h, const int32_t* offsets, int64_t rows_total, int64_t max_rows, int64_t E,
+         int64_t H, int64_t I, const void* blocks, const void* scales, const void* bias,
+         int bias_dtype, void* y, int algo, cudaStream_t st) {
+  BS_TRY(check_expert_args("bs_moe_down", h, blocks, scales, y, rows_total, E, I, H, bias_dtype,
+                           algo));
+  BS_ARG(offsets, "bs_moe_down: null expert_offsets");
+  if (rows_total == 0) return BS_OK;
+  BS_TRY(check_device());
+  const int a = pick_algo(algo, rows_total, E);
+  const int bf32 = bias_dtype == BS_F32;
+  if (a == BS_ALGO_GEMV)
+    return gemv_plain_launch(h, offsets, rows_total, E, I, H, blocks, scales, bias, bf32, y, st);
+  return tc_grouped_launch(1, h, offsets, rows_total, max_rows, E, I, H, blocks, scales, bias,
+                           bf32, 0.f, 0.f, y, st);
+}
+
+struct Workspace {
+  float* logits;
+  void* dispatch;
+  size_t dispatch_bytes;
+  int32_t* offsets;
+  int32_t* row_of_slot;
+  int32_t* token_of_row;
+  void* x_perm;
+  void* h;
+  void* y;
+  size_t total;
+};
+
+Workspace carve(void* base, int64_t T, int64_t H, int64_t I, int64_t E, int64_t k) {
+  Workspace w{};
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = o;
+    o = align_up(o + bytes, 256);
+    return base ? static_cast<char*>(base) + at : nullptr;
+  };
+  const int64_t S = T * k;
+  w.logits = reinterpret_cast<float*>(take((size_t)T * E * sizeof(float)));
+  w.dispatch_bytes = dispatch_workspace_bytes(T, k, E);
+  w.dispatch = take(w.dispatch_bytes);
+  w.offsets = reinterpret_cast<int32_t*>(take((size_t)(E + 1) * sizeof(int32_t)));
+  w.row_of_slot = reinterpret_cast<int32_t*>(take((size_t)S * sizeof(int32_t)));
+  w.token_of_row = reinterpret_cast<int32_t*>(take((size_t)S * sizeof(int32_t)));
+  w.x_perm = take((size_t)S * H * 2);
+  w.h = take((size_t)S * I * 2);
+  w.y = take((size_t)S * H * 2);
+  w.total = o;
+  return w;
+}
+
+}  // namespace bs
+
+extern "C" int bs_moe_gate_up(const void* x_perm, const int32_t* expert_offsets, int64_t rows_total,
+                              int64_t max_rows_per_expert, int64_t E, int64_t H, int64_t I,
+                              const void* blocks, const void* scales, const void* bias,
+                              int bias_dtype, float alpha, float limit, void* h, int algo,
+                              void* stream) {
+  return bs::gate_up(x_perm, expert_offsets, rows_total, max_rows_per_expert, E, H, I, blocks,
+                     scales, bias, bias_dtype, alpha, limit, h, algo,
+                     reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int bs_moe_down(const void* h, const int32_t* expert_offsets, int64_t rows_total,
+                           int64_t max_rows_per_expert, int64_t E, int64_t H, int64_t I,
+                           const void* blocks, const void* scales, const void* bias, int bias_dtype,
+                           void* y, int algo, void* stream) {
+  return bs::down(h, expert_offsets, rows_total, max_rows_per_expert, E, H, I, blocks, scales, bias,
+                  bias_dtype, y, algo, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int bs_mxfp4_matmul(const void* x, int64_t m, int64_t K, const void* blocks,
+                               const void* scales, int64_t N, const void* bias, void* out, int algo,
+                               void* stream) {
+  using namespace bs;
+  BS_TRY(check_expert_args("bs_mxfp4_matmul", x, blocks, scales, out, m, 1, K, N, BS_BF16, algo));
+  if (m == 0) return BS_OK;
+  BS_TRY(check_device());
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int a = pick_algo(algo, m, 1);
+  if (a == BS_ALGO_GEMV)
+    return gemv_plain_launch(x, nullptr, m, 1, K, N, blocks, scales, bias, 0, out, st);
+  return tc_grouped_launch(1, x, nullptr, m, m, 1, K, N, blocks, scales, bias, 0, 0.f, 0.f, out, st);
+}
+
+extern "C" size_t bs_moe_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t k) {
+  return bs::carve(nullptr, T, H, I, E, k).total;
+}
+
+extern "C" int bs_moe_forward(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, int64_t k,
+                              const void* router_weight, const void* router_bias, int router_dtype,
+                              float* scores, int32_t* indices, const void* gate_up_blocks,
+                              const void* gate_up_scales, const void* gate_up_bias,
+                              const void* down_blocks, const void* down_scales,
+                              const void* down_bias, int bias_dtype, float alpha, float limit,
+                              void* out, void* workspace, size_t workspace_bytes, int algo,
+                              void* stream) {
+  using namespace bs;
+  BS_ARG(x && scores && indices && out, "bs_moe_forward: null pointer");
+  BS_ARG(T >= 0 && H > 0 && I > 0 && E > 0 && k > 0 && k <= E, "bs_moe_forward: bad sizes");
+  BS_ARG((router_weight == nullptr) == (router_bias == nullptr),
+         "bs_moe_forward: router weight and bias go together");
+  if (T == 0) return BS_OK;
+  const Workspace w = carve(workspace, T, H, I, E, k);
+  BS_ARG(workspace, "bs_moe_forward: null workspace");
+  BS_REQUIRE(workspace_bytes >= w.total, BS_ERR_CAPACITY,
+             "bs_moe_forward: workspace of %zu bytes is smaller than the %zu needed",
+             workspace_bytes, w.total);
+  BS_ALIGNED16(workspace, "workspace");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (router_weight)
+    BS_TRY(router_launch(x, BS_BF16, router_weight, router_bias, router_dtype, T, H, E, k, w.logits,
+                         scores, indices, BS_I32, st));
+  BS_TRY(dispatch_launch(indices, BS_I32, T, k, E, x, H, w.offsets, w.row_of_slot, w.token_of_row,
+                         w.x_perm, w.dispatch, w.dispatch_bytes, st));
+  const int64_t S = T * k;
+  BS_TRY(gate_up(w.x_perm, w.offsets, S, S, E, H, I, gate_up_blocks, gate_up_scales, gate_up_bias,
+                 bias_dtype, alpha, limit, w.h, algo, st));
+  BS_TRY(down(w.h, w.offsets, S, S, E, H, I, down_blocks, down_scales, down_bias, bias_dtype, w.y,
+              algo, st));
+  BS_TRY(combine_launch(w.y, w.row_of_slot, scores, T, k, H, out, st));
+  return BS_OK;
+}

@@ -1,0 +1,401 @@
+// Grouped expert GEMM on the 5th-generation tensor cores (tcgen05, sm_100a).
+//
+// Replaces the per-expert loop of block_streamer/gptoss.py:149-176 at prefill
+// shapes: for every expert e, out[rows of e] = epilogue(X[rows of e] @ W[e]^T)
+// with W[e] the MXFP4 weight [Nw, K] (checkpoint layout, K-contiguous).
+//
+// Formulation ("swap AB"): the MMA's M side is 128 WEIGHT rows, its N side is up
+// to 320 TOKEN rows of one expert, so at uniform routing every weight byte is
+// fetched and dequantized once per layer.
+//   * A (weights): TMA brings the packed e2m1 bytes of a 128x64 slice into
+//     shared memory; four dequant warps decode them (bit-exact with the
+//     reference's LUT + ldexp) and write bf16 straight into TENSOR MEMORY with
+//     tcgen05.st — the MMA reads A from TMEM ("TS" form), so the dequantized
+//     weights never touch shared memory.
+//   * B (tokens): 128B-swizzled TMA tiles of 64 x 64 bf16 in shared memory.
+//   * D: fp32 accumulators in TMEM (up to 320 columns: one 128x256 and one
+//     128x64 MMA per K16 step), drained by four epilogue warps with tcgen05.ld.
+// Warp roles (320 threads): 0 TMA producer, 1 MMA issuer (+TMEM owner),
+// 2-5 epilogue, 6-9 dequant.  A 4-stage mbarrier pipeline links them; every
+// wait is bounded (timeout -> status word + clean exit, TMEM freed).
+// MODE 0: gate_up — bias + clamped interleaved SwiGLU (gptoss.py:130-135,158-166).
+// MODE 1: plain   — bias (gptoss.py:167-174) / mxfp4_matmul.
+#include <cudaTypedefs.h>
+
+#include "bs_common.cuh"
+#include "bs_ptx.cuh"
+
+namespace bs {
+namespace {
+
+constexpr int kBM = 128;                      // weight rows per tile (MMA M)
+constexpr int kBK = 64;                       // K per pipeline stage
+constexpr int kNMax = 320;                    // token rows per tile
+constexpr int kStages = 4;
+constexpr int kBoxRows = 64;                  // token rows per TMA box
+constexpr int kBoxBytes = kBoxRows * kBK * 2;  // 8 KiB
+constexpr int kBBytes = kNMax * kBK * 2;      // 40 KiB
+constexpr int kABytes = kBM * kBK / 2;        // 4 KiB of e2m1 bytes
+constexpr int kStageBytes = kBBytes + kABytes;
+constexpr int kACol = 320;                    // TMEM column of the A ring
+constexpr int kTmemCols = 512;
+constexpr int kThreads = 320;
+constexpr int kWarpTMA = 0, kWarpMMA = 1, kWarpEpi0 = 2, kWarpDeq0 = 6;
+constexpr int kNumBars = 3 * kStages + 3;     // full, adone, empty per stage; accfull, accempty, drain
+
+static_assert(kStageBytes % 1024 == 0, "stages must keep 1024-byte alignment for SW128");
+static_assert(kACol + kStages * (kBK / 2) <= kTmemCols, "TMEM budget");
+
+struct Tile {
+  int e, mt, nrows, nmma;
+  int64_t r0;
+};
+
+__device__ __forceinline__ int nchunks_of(int n) { return n > 0 ? (n + kNMax - 1) / kNMax : 0; }
+
+__device__ void build_sched(const int* __restrict__ offsets, int64_t rows_total, int E, int MT,
+                            int* off, int* ipre) {
+  const int tid = threadIdx.x;
+  for (int e = tid; e <= E; e += blockDim.x)
+    off[e] = offsets ? offsets[e] : (e == 0 ? 0 : (int)rows_total);
+  __syncthreads();
+  if (tid < 32) {
+    const int per = (E + 31) / 32;
+    const int e0 = tid * per, e1 = min(E, e0 + per);
+    int sum = 0;
+    for (int e = e0; e < e1; ++e) sum += nchunks_of(off[e + 1] - off[e]) * MT;
+    int incl = sum;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (tid >= o) incl += v;
+    }
+    int run = incl - sum;
+    for (int e = e0; e < e1; ++e) {
+      ipre[e] = run;
+      run += nchunks_of(off[e + 1] - off[e]) * MT;
+    }
+    if (tid == 31) ipre[E] = incl;
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ Tile decode_item(const int* off, const int* ipre, int E, int MT, int item) {
+  int lo = 0, hi = E - 1;  // largest e with ipre[e] <= item (skips experts without rows)
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (ipre[mid] <= item) lo = mid; else hi = mid - 1;
+  }
+  Tile t;
+  t.e = lo;
+  const int local = item - ipre[lo];
+  const int c = local / MT;
+  t.mt = local - c * MT;
+  const int n = off[lo + 1] - off[lo];
+  const int nch = nchunks_of(n);
+  const int a = (int)(((int64_t)c * n) / nch), b = (int)(((int64_t)(c + 1) * n) / nch);
+  t.r0 = off[lo] + a;
+  t.nrows = b - a;
+  t.nmma = (t.nrows + 15) & ~15;
+  return t;
+}
+
+__device__ __forceinline__ uint32_t load_scale_pair(const uint8_t* srow, int g0, int G, bool valid) {
+  uint32_t a = 127u, b = 127u;
+  if (valid && g0 < G) a = __ldg(srow + g0);
+  if (valid && g0 + 1 < G) b = __ldg(srow + g0 + 1);
+  return a | (b << 8);
+}
+
+__device__ __forceinline__ float bias_at(const void* bias, int f32, int64_t i) {
+  if (!bias) return 0.f;
+  return f32 ? static_cast<const float*>(bias)[i]
+             : __bfloat162float(static_cast<const __nv_bfloat16*>(bias)[i]);
+}
+
+// all lanes wait; the warp proceeds only if every lane saw the phase complete
+__device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatile int* abort) {
+  const bool ok = ptx::mbar_wait(bar, parity, abort);
+  return __all_sync(0xffffffffu, ok);
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kThreads, 1) tc_grouped_kernel(
+    const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_a,
+    const uint8_t* __restrict__ scales, const int* __restrict__ offsets, int64_t rows_total,
+    int E, int K, int Nw, const void* __restrict__ bias, int bias_f32, float alpha, float limit,
+    uint16_t* __restrict__ out, int* status) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + kNumBars);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  int* off = reinterpret_cast<int*>(tmem_holder + 2);
+  int* ipre = off + (E + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  auto bar = [&](int i) { return ptx::smem_addr(bars + i); };
+  auto full = [&](int s) { return bar(s); };
+  auto adone = [&](int s) { return bar(kStages + s); };
+  auto empty = [&](int s) { return bar(2 * kStages + s); };
+  const uint32_t accfull = bar(3 * kStages), accempty = bar(3 * kStages + 1),
+                 drain = bar(3 * kStages + 2);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      ptx::mbar_init(full(s), 1);
+      ptx::mbar_init(adone(s), 4);
+      ptx::mbar_init(empty(s), 1);
+    }
+    ptx::mbar_init(accfull, 1);
+    ptx::mbar_init(accempty, 4);
+    ptx::mbar_init(drain, 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == kWarpTMA && lane == 0) {
+    ptx::tma_prefetch_desc(&tm_b);
+    ptx::tma_prefetch_desc(&tm_a);
+  }
+  if (warp == kWarpMMA) {
+    ptx::tmem_alloc(ptx::smem_addr(tmem_holder), kTmemCols);
+    ptx::tmem_relinquish();
+  }
+  const int MT = (Nw + kBM - 1) / kBM;
+  build_sched(offsets, rows_total, E, MT, off, ipre);  // contains __syncthreads
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tbase = *tmem_holder;
+  const int KS = (K + kBK - 1) / kBK;
+  const int G = K / 32;
+  const int total = ipre[E];
+
+  if (warp == kWarpTMA) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int last_round[kStages];
+      for (int s = 0; s < kStages; ++s) last_round[s] = -1;
+      uint32_t g = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; ok && item < total; item += gridDim.x) {
+        const Tile t = decode_item(off, ipre, E, MT, item);
+        const int nbox = (t.nmma + kBoxRows - 1) / kBoxRows;
+        const int arow = t.e * Nw + t.mt * kBM;
+        for (int ks = 0; ks < KS; ++ks, ++g) {
+          const int s = g % kStages, r = g / kStages;
+          if (!ptx::mbar_wait(empty(s), (r & 1) ^ 1, abort_flag)) { ok = false; break; }
+          uint8_t* st = smem + s * kStageBytes;
+          ptx::mbar_arrive_expect_tx(full(s), nbox * kBoxBytes + kABytes);
+          for (int jb = 0; jb < nbox; ++jb)
+            ptx::tma_load_2d(ptx::smem_addr(st + jb * kBoxBytes), &tm_b, full(s), ks * kBK,
+                             (int)(t.r0 + jb * kBoxRows));
+          ptx::tma_load_2d(ptx::smem_addr(st + kBBytes), &tm_a, full(s), ks * (kBK / 2), arow);
+          last_round[s] = r;
+        }
+      }
+      if (!ok) {  // let issued copies land before the CTA exits
+        for (int s = 0; s < kStages; ++s)
+          if (last_round[s] >= 0) ptx::mbar_wait(full(s), last_round[s] & 1, abort_flag, 200000000LL);
+      }
+    }
+    __syncwarp();
+  } else if (warp == kWarpMMA) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      uint32_t g = 0, j = 0;
+      bool ok = true;
+      bool issued = false;
+      for (int item = blockIdx.x; ok && item < total; item += gridDim.x, ++j) {
+        const Tile t = decode_item(off, ipre, E, MT, item);
+        const uint32_t n1 = t.nmma < 256 ? t.nmma : 256, n2 = t.nmma - n1;
+        const uint32_t id1 = ptx::idesc_bf16_f32(kBM, n1);
+        const uint32_t id2 = n2 ? ptx::idesc_bf16_f32(kBM, n2) : 0u;
+        if (!ptx::mbar_wait(accempty, (j & 1) ^ 1, abort_flag)) { ok = false; break; }
+        ptx::tc_fence_after();
+        for (int ks = 0; ks < KS; ++ks, ++g) {
+          const int s = g % kStages;
+          const uint32_t ph = (g / kStages) & 1;
+          if (!ptx::mbar_wait(full(s), ph, abort_flag) || !ptx::mbar_wait(adone(s), ph, abort_flag)) {
+            ok = false;
+            break;
+          }
+          ptx::tc_fence_after();
+          const uint32_t bsm = ptx::smem_addr(smem + s * kStageBytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            const uint32_t acc = (ks > 0 || kk > 0) ? 1u : 0u;
+            const uint32_t a_t = tbase + kACol + s * (kBK / 2) + kk * 8;
+            ptx::mma_ts_bf16(tbase, a_t, ptx::sdesc_kmajor_sw128(bsm + kk * 32), id1, acc);
+            if (n2) ptx::mma_ts_bf16(tbase + 256, a_t, ptx::sdesc_kmajor_sw128(bsm + 256 * 128 + kk * 32),
+                                     id2, acc);
+          }
+          ptx::tc_commit(empty(s));
+          issued = true;
+        }
+        if (!ok) break;
+        ptx::tc_commit(accfull);
+      }
+      if (!ok && issued) {  // every issued MMA must finish before TMEM is freed
+        ptx::tc_commit(drain);
+        ptx::mbar_wait(drain, 0, abort_flag, 200000000LL);
+      }
+    }
+    __syncwarp();
+  } else if (warp < kWarpDeq0) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    uint32_t j = 0;
+    for (int item = blockIdx.x; item < total; item += gridDim.x, ++j) {
+      const Tile t = decode_item(off, ipre, E, MT, item);
+      if (!warp_wait(accfull, j & 1, abort_flag)) break;
+      ptx::tc_fence_after();
+      const int row_w = t.mt * kBM + q * 32 + lane;
+      const bool rv = row_w < Nw;
+      const float bv = rv ? bias_at(bias, bias_f32, (int64_t)t.e * Nw + row_w) : 0.f;
+      const uint32_t taddr = tbase + ((uint32_t)(q * 32) << 16);
+      for (int c0 = 0; c0 < t.nmma; c0 += 16) {
+        uint32_t v[16];
+        ptx::tmem_ld_32x32b_x16(taddr + c0, v);
+        ptx::tmem_wait_ld();
+        if (MODE == 0) {
+          const float bp = __shfl_xor_sync(0xffffffffu, bv, 1);
+          const int odd = lane & 1;
+          const int Iout = Nw / 2;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const uint32_t pv = __shfl_xor_sync(0xffffffffu, v[i], 1);
+            const int n = c0 + i;
+            if ((i & 1) == odd && n < t.nrows && rv) {
+              const float own = __uint_as_float(v[i]) + bv;
+              const float oth = __uint_as_float(pv) + bp;
+              const float hv = odd ? swiglu(oth, own, alpha, limit) : swiglu(own, oth, alpha, limit);
+              out[(t.r0 + n) * Iout + (row_w >> 1)] = __bfloat16_as_ushort(__float2bfloat16_rn(hv));
+            }
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int n = c0 + i;
+            if (n < t.nrows && rv)
+              out[(t.r0 + n) * Nw + row_w] =
+                  __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[i]) + bv));
+          }
+        }
+      }
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(accempty);
+    }
+  } else {
+    // ------------------------------------------------------------ dequant (A -> TMEM)
+    const int q = warp & 3;
+    const int r = q * 32 + lane;  // TMEM lane == row within the weight tile
+    const uint32_t taddr = tbase + ((uint32_t)(q * 32) << 16) + kACol;
+    uint32_t g = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; ok && item < total; item += gridDim.x) {
+      const Tile t = decode_item(off, ipre, E, MT, item);
+      const int row_w = t.mt * kBM + r;
+      const bool rv = row_w < Nw;
+      const uint8_t* srow = scales + ((int64_t)t.e * Nw + (rv ? row_w : 0)) * G;
+      uint32_t sc_next = load_scale_pair(srow, 0, G, rv);
+      uint32_t sc_next2 = load_scale_pair(srow, 2, G, rv);
+      for (int ks = 0; ks < KS; ++ks, ++g) {
+        const uint32_t sc = sc_next;
+        sc_next = sc_next2;
+        sc_next2 = load_scale_pair(srow, 2 * (ks + 2), G, rv);
+        const int s = g % kStages;
+        const uint32_t ph = (g / kStages) & 1;
+        if (!warp_wait(full(s), ph, abort_flag)) { ok = false; break; }
+        const uint4* src = reinterpret_cast<const uint4*>(smem + s * kStageBytes + kBBytes + r * 32);
+        const uint4 b0 = src[0], b1 = src[1];
+        const uint32_t s0 = sc & 0xFFu, s1 = sc >> 8;
+        const E2M1Pool p0 = make_e2m1_pool(s0), p1 = make_e2m1_pool(s1);
+        uint32_t v[32];
+        e2m1x8_decode(b0.x, s0, p0, v + 0);
+        e2m1x8_decode(b0.y, s0, p0, v + 4);
+        e2m1x8_decode(b0.z, s0, p0, v + 8);
+        e2m1x8_decode(b0.w, s0, p0, v + 12);
+        e2m1x8_decode(b1.x, s1, p1, v + 16);
+        e2m1x8_decode(b1.y, s1, p1, v + 20);
+        e2m1x8_decode(b1.z, s1, p1, v + 24);
+        e2m1x8_decode(b1.w, s1, p1, v + 28);
+        ptx::tmem_st_32x32b_x32(taddr + s * (kBK / 2), v);
+        ptx::tmem_wait_st();
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(adone(s));
+      }
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort_flag) record_status(status, BS_ERR_TIMEOUT);
+  if (warp == kWarpMMA) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tbase, kTmemCols);
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+int make_map_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner,
+                uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+                CUtensorMapSwizzle sw) {
+  auto fn = encode_fn();
+  BS_REQUIRE(fn, BS_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  BS_REQUIRE(r == CUDA_SUCCESS, BS_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+  return BS_OK;
+}
+
+}  // namespace
+
+int tc_grouped_launch(int mode, const void* x, const int32_t* offsets, int64_t rows_total,
+                      int64_t max_rows_per_expert, int64_t E, int64_t K, int64_t N,
+                      const void* blocks, const void* scales, const void* bias, int bias_f32,
+                      float alpha, float limit, void* out, cudaStream_t st) {
+  (void)max_rows_per_expert;
+  BS_ARG(E * N < (int64_t)INT32_MAX && rows_total + kNMax < (int64_t)INT32_MAX,
+         "tcgen05 GEMM: sizes exceed 32-bit TMA coordinates");
+  BS_ARG(mode == 1 || N % 2 == 0, "tcgen05 GEMM: gate_up rows must be even");
+  BS_ARG(offsets || E == 1, "tcgen05 GEMM: expert_offsets required");
+  const int64_t G = K / 32;
+  CUtensorMap tm_b, tm_a;
+  BS_TRY(make_map_2d(&tm_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)rows_total,
+                     (uint64_t)K * 2, kBK, kBoxRows, CU_TENSOR_MAP_SWIZZLE_128B));
+  BS_TRY(make_map_2d(&tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, blocks, (uint64_t)G * 16, (uint64_t)(E * N),
+                     (uint64_t)G * 16, kBK / 2, kBM, CU_TENSOR_MAP_SWIZZLE_NONE));
+  const size_t smem = 1024 + (size_t)kStages * kStageBytes + kNumBars * 8 + 16 +
+                      (size_t)2 * (E + 1) * sizeof(int);
+  BS_REQUIRE(smem <= 227 * 1024, BS_ERR_CAPACITY, "tcgen05 GEMM: too many experts for shared memory");
+  auto kern = mode == 0 ? tc_grouped_kernel<0> : tc_grouped_kernel<1>;
+  BS_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  const int grid = sm_count();
+  kern<<<grid, kThreads, smem, st>>>(tm_b, tm_a, static_cast<const uint8_t*>(scales), offsets,
+                                     rows_total, (int)E, (int)K, (int)N, bias, bias_f32, alpha,
+                                     limit, static_cast<uint16_t*>(out), device_status_ptr());
+  BS_LAUNCHED();
+  return BS_OK;
+}
+
+}  // namespace bs

@@ -1,0 +1,190 @@
+"""Drop-in gpt-oss MoE modules backed by the sm_100a kernels.
+
+Mirrors ``block_streamer/gptoss.py`` (hareramray/BlockStreamer) and the
+transformers gpt-oss MLP it plugs into:
+
+* ``dequantize_expert`` / ``mxfp4_matmul``       — gptoss.py:24-42, 45-75
+* ``B200MXFP4Experts``                           — gptoss.py:78-177 (``MXFP4Experts``)
+* ``install_b200_experts``                       — gptoss.py:180-189 (``install_mxfp4_experts``)
+* ``B200GptOssMLP`` / ``install_b200_mlp``       — transformers models/gpt_oss/
+  modeling_gpt_oss.py:117-146 (``GptOssTopKRouter`` + ``GptOssMLP``) with the
+  experts above, as one fused layer.
+
+Parameter names, shapes and dtypes are the checkpoint's, so
+``StreamedModel``'s ``functional_call(..., strict=True)`` binds staged state to
+these modules unchanged.  The modules read ``data_ptr()`` on every call, launch
+on the current stream, allocate workspaces with the caching allocator and
+never mutate their parameters.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch import Tensor, nn
+
+from . import kernels
+
+
+def dequantize_expert(blocks: Tensor, scales: Tensor, dtype: torch.dtype = torch.bfloat16) -> Tensor:
+    """Dequantize one expert's packed MXFP4 weight to a dense [groups*32, rows] matrix.
+
+    Same contract as the reference (gptoss.py:24-42): ``blocks`` is
+    [1, rows, groups, 16] uint8 and ``scales`` [1, rows, groups]; a missing
+    leading expert dimension raises ``ValueError``.  Bit-exact with the
+    reference for every byte and scale.
+    """
+    if blocks.dim() != 4:
+        raise ValueError(f"Expected [1, rows, groups, 16] packed blocks, got {tuple(blocks.shape)}")
+    dense = kernels.dequant_mxfp4(blocks, scales, transpose=True)
+    if dtype != torch.bfloat16:
+        # every dequantized value has at most two significant bits, so the bf16
+        # result converts exactly to wider float types
+        dense = dense.to(dtype)
+    return dense.squeeze(0)
+
+
+class _MXFP4Matmul(torch.autograd.Function):
+    """x @ dequantize(blocks, scales) without keeping the dense weight.
+
+    Forward runs the fused dequant-GEMM kernel.  Backward (dL/dx) re-derives the
+    dense weight with the dequant kernel and multiplies by its transpose, as the
+    reference does (gptoss.py:64-71).
+    """
+
+    @staticmethod
+    def forward(ctx, x: Tensor, blocks: Tensor, scales: Tensor) -> Tensor:
+        ctx.save_for_backward(blocks, scales)
+        ctx.x_dtype = x.dtype
+        lead = x.shape[:-1]
+        out = kernels.mxfp4_matmul(x.reshape(-1, x.shape[-1]).to(torch.bfloat16).contiguous(),
+                                   blocks.squeeze(0), scales.squeeze(0))
+        return out.reshape(*lead, out.shape[-1]).to(x.dtype)
+
+    @staticmethod
+    def backward(ctx, grad: Tensor):
+        blocks, scales = ctx.saved_tensors
+        grad_x = None
+        if ctx.needs_input_grad[0]:
+            weight = dequantize_expert(blocks, scales, grad.dtype)
+            grad_x = grad @ weight.transpose(-2, -1)
+        return grad_x, None, None
+
+
+def mxfp4_matmul(x: Tensor, blocks: Tensor, scales: Tensor) -> Tensor:
+    """gptoss.py:74-75: ``x @ dequantize_expert(blocks, scales)`` for blocks [1, N, G, 16]."""
+    if blocks.dim() != 4:
+        raise ValueError(f"Expected [1, rows, groups, 16] packed blocks, got {tuple(blocks.shape)}")
+    return _MXFP4Matmul.apply(x, blocks, scales)
+
+
+def _packed(experts: int, rows: int, groups: int) -> nn.Parameter:
+    return nn.Parameter(torch.empty(experts, rows, groups, 16, dtype=torch.uint8, device="meta"),
+                        requires_grad=False)
+
+
+def _scales(experts: int, rows: int, groups: int) -> nn.Parameter:
+    return nn.Parameter(torch.empty(experts, rows, groups, dtype=torch.uint8, device="meta"),
+                        requires_grad=False)
+
+
+class B200MXFP4Experts(nn.Module):
+    """Drop-in for ``MXFP4Experts`` / ``GptOssExperts`` running the fused kernels.
+
+    ``forward(hidden_states [T,H], router_indices [T,k], routing_weights [T,k]) -> [T,H]``
+    (gptoss.py:137-142).  Parameters (gptoss.py:115-128) are created on ``meta``
+    and bound by the caller (``functional_call``, ``load_state_dict(assign=True)``
+    or ``.to_empty``).  The down projection's group count is I/32; the reference
+    uses H/32 for both (gptoss.py:92), which is the same for gpt-oss (I == H).
+    """
+
+    def __init__(self, config, dtype: torch.dtype = torch.bfloat16, algo: int = kernels.ALGO_AUTO) -> None:
+        super().__init__()
+        self.num_experts = config.num_local_experts
+        self.hidden_size = config.hidden_size
+        self.expert_dim = config.intermediate_size
+        self.alpha = 1.702
+        self.limit = getattr(config, "swiglu_limit", 7.0)
+        self.algo = algo
+        E, H, I = self.num_experts, self.hidden_size, self.expert_dim
+        self.gate_up_proj_blocks = _packed(E, 2 * I, H // 32)
+        self.gate_up_proj_scales = _scales(E, 2 * I, H // 32)
+        self.gate_up_proj_bias = nn.Parameter(torch.empty(E, 2 * I, dtype=dtype, device="meta"),
+                                              requires_grad=False)
+        self.down_proj_blocks = _packed(E, H, I // 32)
+        self.down_proj_scales = _scales(E, H, I // 32)
+        self.down_proj_bias = nn.Parameter(torch.empty(E, H, dtype=dtype, device="meta"),
+                                           requires_grad=False)
+
+    def forward(self, hidden_states: Tensor, router_indices: Tensor | None = None,
+                routing_weights: Tensor | None = None) -> Tensor:
+        if router_indices is None or routing_weights is None:
+            raise ValueError("B200MXFP4Experts needs router_indices and routing_weights")
+        k = router_indices.shape[-1]
+        out, _, _ = kernels.moe_forward(
+            hidden_states.to(torch.bfloat16), self.gate_up_proj_blocks, self.gate_up_proj_scales,
+            self.gate_up_proj_bias, self.down_proj_blocks, self.down_proj_scales,
+            self.down_proj_bias, k, indices=router_indices, scores=routing_weights,
+            alpha=self.alpha, limit=self.limit, algo=self.algo)
+        return out.to(hidden_states.dtype)
+
+
+class _Router(nn.Module):
+    """Holds ``router.weight`` [E,H] and ``router.bias`` [E] under the HF names."""
+
+    def __init__(self, experts: int, hidden: int, dtype: torch.dtype) -> None:
+        super().__init__()
+        self.weight = nn.Parameter(torch.empty(experts, hidden, dtype=dtype, device="meta"))
+        self.bias = nn.Parameter(torch.empty(experts, dtype=dtype, device="meta"))
+
+
+class B200GptOssMLP(nn.Module):
+    """Drop-in for transformers' ``GptOssMLP`` with packed experts.
+
+    ``forward(hidden_states [B,S,H]) -> (out [B,S,H], router_scores [B*S,k])``
+    (modeling_gpt_oss.py:140-146): router (fp32 accumulate, top-k, softmax over
+    the k), dispatch, gate_up + SwiGLU, down, weighted combine — all on the GPU
+    with no host synchronization.  ``router_scores`` has the router's dtype.
+    """
+
+    def __init__(self, config, dtype: torch.dtype = torch.bfloat16,
+                 router_dtype: torch.dtype = torch.float32, algo: int = kernels.ALGO_AUTO) -> None:
+        super().__init__()
+        self.top_k = config.num_experts_per_tok
+        self.router = _Router(config.num_local_experts, config.hidden_size, router_dtype)
+        self.experts = B200MXFP4Experts(config, dtype, algo)
+
+    def forward(self, hidden_states: Tensor):
+        B, S, H = hidden_states.shape
+        x = hidden_states.reshape(-1, H).to(torch.bfloat16)
+        ex = self.experts
+        out, scores, _ = kernels.moe_forward(
+            x, ex.gate_up_proj_blocks, ex.gate_up_proj_scales, ex.gate_up_proj_bias,
+            ex.down_proj_blocks, ex.down_proj_scales, ex.down_proj_bias, self.top_k,
+            router_weight=self.router.weight, router_bias=self.router.bias,
+            alpha=ex.alpha, limit=ex.limit, algo=ex.algo)
+        return out.reshape(B, S, H).to(hidden_states.dtype), scores.to(self.router.weight.dtype)
+
+
+def install_b200_experts(model: nn.Module, config, dtype=torch.bfloat16) -> int:
+    """Swap every ``GptOssExperts`` / ``MXFP4Experts`` for ``B200MXFP4Experts``
+    (the counterpart of gptoss.py:180-189)."""
+    replaced = 0
+    for layer in model.model.layers:
+        name = type(layer.mlp.experts).__name__
+        if name in ("GptOssExperts", "MXFP4Experts"):
+            layer.mlp.experts = B200MXFP4Experts(config, dtype)
+            replaced += 1
+    return replaced
+
+
+def install_b200_mlp(model: nn.Module, config, dtype=torch.bfloat16,
+                     router_dtype: torch.dtype | None = None) -> int:
+    """Swap every ``GptOssMLP`` for ``B200GptOssMLP`` (router + experts fused).
+    Parameter names (``mlp.router.*``, ``mlp.experts.*``) are unchanged."""
+    replaced = 0
+    for layer in model.model.layers:
+        if type(layer.mlp).__name__ == "GptOssMLP":
+            rd = router_dtype or layer.mlp.router.weight.dtype
+            layer.mlp = B200GptOssMLP(config, dtype, rd)
+            replaced += 1
+    return replaced

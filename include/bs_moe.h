@@ -1,0 +1,153 @@
+/*
+ * bs_moe.h — C ABI of the B200 (sm_100a) gpt-oss mixture-of-experts layer.
+ *
+ * The reference (hareramray/BlockStreamer) is pure Python: its MoE layer is
+ * transformers' GptOssMLP with block_streamer.gptoss.MXFP4Experts swapped in.
+ * Each entry point below replaces one step of that Python path; the comment on
+ * each names the reference lines it replaces.  The Python package
+ * blockstreamer_b200 binds these with ctypes and keeps the reference's module
+ * API (parameter names, shapes, dtypes) on top.
+ *
+ * Conventions
+ *  - Every pointer is a DEVICE pointer unless stated otherwise; sizes are int64.
+ *  - `stream` is a cudaStream_t passed as void*; NULL means the legacy stream.
+ *    Every call is asynchronous on `stream` unless stated otherwise.
+ *  - Return value: BS_OK (0) or a BS_ERR_* code; bs_last_error_string() gives
+ *    the message of the last failure on the calling host thread.
+ *  - Tensors are dense, row-major, without padding.  Rows handled by 128-bit or
+ *    TMA loads must start on 16-byte boundaries (checked: BS_ERR_MISALIGNED).
+ *  - Packed expert weights use the checkpoint layout:
+ *      blocks [E, rows, G, 16] uint8  (two e2m1 codes per byte, low nibble first)
+ *      scales [E, rows, G]     uint8  (e8m0, value 2^(s-127))
+ *    with G = K / 32 groups along the contraction dimension K.
+ *  - Permuted ("dispatched") rows are grouped by expert: expert e owns rows
+ *    [expert_offsets[e], expert_offsets[e+1]) of x_perm / h / y.
+ */
+#ifndef BS_MOE_H
+#define BS_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum bs_status {
+  BS_OK = 0,
+  BS_ERR_INVALID_ARGUMENT = 1, /* null pointer, bad shape or dtype code            */
+  BS_ERR_MISALIGNED = 2,       /* a pointer or row pitch is not 16-byte aligned     */
+  BS_ERR_CAPACITY = 3,         /* workspace too small / size beyond a fixed maximum */
+  BS_ERR_CUDA = 4,             /* a CUDA runtime call failed                        */
+  BS_ERR_TIMEOUT = 5,          /* a bounded device-side wait ran out (see status)   */
+  BS_ERR_UNSUPPORTED = 6       /* device is not sm_100 / feature not built          */
+};
+
+enum bs_dtype { BS_BF16 = 0, BS_F32 = 1, BS_I32 = 2, BS_I64 = 3 };
+
+enum bs_algo {
+  BS_ALGO_AUTO = 0,     /* pick by tokens per expert                                  */
+  BS_ALGO_GEMV = 1,     /* CUDA-core dequant-GEMV (decode shapes, HBM-bound)          */
+  BS_ALGO_TCGEN05 = 2   /* tcgen05/TMEM grouped GEMM (prefill shapes)                 */
+};
+
+/* Library identity. */
+int bs_version(void);
+const char* bs_last_error_string(void);
+
+/* Reads (and with clear != 0, resets) the device status word of the current
+ * device: 0 when no kernel reported a problem, else the first BS_ERR_* a kernel
+ * recorded (e.g. BS_ERR_TIMEOUT from a bounded mbarrier wait).  Synchronizes
+ * `stream`.  Host-side out pointer. */
+int bs_device_status(int* out_status, int clear, void* stream);
+
+/* MXFP4 -> bf16 dequantization.
+ * Replaces block_streamer/gptoss.py:24-42 (dequantize_expert), which calls
+ * transformers integrations/mxfp4.py:333-355 (convert_moe_packed_tensors).
+ * out: [E, G*32, rows] bf16 when transpose != 0 (the reference's orientation),
+ *      [E, rows, G*32] otherwise.  Bit-exact with the reference for every byte
+ *      and scale value (exact product, +-inf beyond the bf16 range). */
+int bs_dequant_mxfp4(const void* blocks, const void* scales, int64_t experts, int64_t rows,
+                     int64_t groups, int transpose, void* out, void* stream);
+
+/* Router: logits = x W^T + b, top-k (descending), softmax over the k values.
+ * Replaces transformers models/gpt_oss/modeling_gpt_oss.py:126-130
+ * (GptOssTopKRouter.forward).  x [T,H] bf16 or f32 (x_dtype); weight [E,H] and
+ * bias [E] f32 or bf16 (w_dtype; bf16 logits are rounded to bf16 before top-k,
+ * as the reference computes them in the weight dtype).  Accumulation is fp32.
+ * logits [T,E] f32 (may be NULL); scores [T,k] f32; indices [T,k] int32/int64. */
+int bs_router(const void* x, int x_dtype, const void* weight, const void* bias, int w_dtype,
+              int64_t T, int64_t H, int64_t E, int64_t k, float* logits, float* scores,
+              void* indices, int index_dtype, void* stream);
+
+/* Workspace bytes bs_dispatch needs for (T, k, E). */
+size_t bs_dispatch_workspace_bytes(int64_t T, int64_t k, int64_t E);
+
+/* Token permutation (dispatch).  Replaces block_streamer/gptoss.py:143-154
+ * (one_hot / nonzero / where / gather), without any host synchronization.
+ * indices [T,k] int32 or int64 (index_dtype) in [0, E).
+ * Outputs: expert_offsets [E+1] int32 (exclusive scan of per-expert row counts;
+ * offsets[E] = T*k), row_of_slot [T*k] int32 (permuted row of slot (t, s)),
+ * token_of_row [T*k] int32, and, when x != NULL, x_perm [T*k, H] bf16 with
+ * x_perm[row_of_slot[t*k+s]] = x[t].  Within an expert, rows follow (token, slot)
+ * order, so the permutation is deterministic. */
+int bs_dispatch(const void* indices, int index_dtype, int64_t T, int64_t k, int64_t E,
+                const void* x, int64_t H, int32_t* expert_offsets, int32_t* row_of_slot,
+                int32_t* token_of_row, void* x_perm, void* workspace, size_t workspace_bytes,
+                void* stream);
+
+/* Grouped gate_up projection + bias + clamped, interleaved SwiGLU.
+ * Replaces block_streamer/gptoss.py:158-166 with _apply_gate (130-135):
+ *   g = x_perm[rows of e] @ dequant(W_gu[e]) + b_gu[e]        (fp32 accumulate)
+ *   gate = min(g[:, 0::2], limit); up = clamp(g[:, 1::2], -limit, limit)
+ *   h = (up + 1) * gate * sigmoid(alpha * gate)               -> bf16 [rows, I]
+ * x_perm [rows_total, H] bf16; blocks [E, 2I, H/32, 16]; scales [E, 2I, H/32];
+ * bias [E, 2I] (bias_dtype bf16 or f32); h [rows_total, I] bf16.
+ * max_rows_per_expert bounds the tile schedule (use rows_total when unknown). */
+int bs_moe_gate_up(const void* x_perm, const int32_t* expert_offsets, int64_t rows_total,
+                   int64_t max_rows_per_expert, int64_t E, int64_t H, int64_t I,
+                   const void* blocks, const void* scales, const void* bias, int bias_dtype,
+                   float alpha, float limit, void* h, int algo, void* stream);
+
+/* Grouped down projection + bias.  Replaces block_streamer/gptoss.py:167-174:
+ *   y = h[rows of e] @ dequant(W_d[e]) + b_d[e]   -> bf16 [rows_total, H]
+ * blocks [E, H, I/32, 16]; scales [E, H, I/32]; bias [E, H]. */
+int bs_moe_down(const void* h, const int32_t* expert_offsets, int64_t rows_total,
+                int64_t max_rows_per_expert, int64_t E, int64_t H, int64_t I, const void* blocks,
+                const void* scales, const void* bias, int bias_dtype, void* y, int algo,
+                void* stream);
+
+/* Weighted combine and un-permute.  Replaces block_streamer/gptoss.py:175-176:
+ *   out[t] = bf16( sum_s weights[t,s] * y[row_of_slot[t*k+s]] )   (fp32 sum)
+ * y [T*k, H] bf16; weights [T,k] f32; out [T,H] bf16. */
+int bs_combine(const void* y, const int32_t* row_of_slot, const float* weights, int64_t T,
+               int64_t k, int64_t H, void* out, void* stream);
+
+/* One expert projection without activation: out[m, N] = x[m, K] @ dequant(W) (+ bias).
+ * Replaces block_streamer/gptoss.py:74-75 (mxfp4_matmul forward) for one expert:
+ * blocks [N, K/32, 16], scales [N, K/32], x [m, K] bf16, out [m, N] bf16;
+ * bias [N] bf16 or NULL. */
+int bs_mxfp4_matmul(const void* x, int64_t m, int64_t K, const void* blocks, const void* scales,
+                    int64_t N, const void* bias, void* out, int algo, void* stream);
+
+/* Whole layer: router (when router weights are given) or caller routing,
+ * dispatch, gate_up+SwiGLU, down, combine.  Replaces GptOssMLP.forward
+ * (modeling_gpt_oss.py:140-146) with MXFP4Experts.forward (gptoss.py:137-177).
+ *  - router_weight/router_bias non-NULL: computes scores/indices into the
+ *    caller's `scores` [T,k] f32 and `indices` [T,k] int32 buffers.
+ *  - router_weight NULL: `scores` and `indices` are inputs.
+ * Workspace: bs_moe_workspace_bytes(T, H, I, E, k). */
+size_t bs_moe_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t k);
+int bs_moe_forward(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, int64_t k,
+                   const void* router_weight, const void* router_bias, int router_dtype,
+                   float* scores, int32_t* indices,
+                   const void* gate_up_blocks, const void* gate_up_scales, const void* gate_up_bias,
+                   const void* down_blocks, const void* down_scales, const void* down_bias,
+                   int bias_dtype, float alpha, float limit, void* out, void* workspace,
+                   size_t workspace_bytes, int algo, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BS_MOE_H */

@@ -45,10 +45,16 @@ def dequant_expert(blocks: torch.Tensor, scales: torch.Tensor, dtype: torch.dtyp
     """
     rows, groups, _ = blocks.shape
     b = blocks.to(torch.int64)
-    vals = torch.empty(rows, groups, 32, dtype=torch.float64)
-    vals[..., 0::2] = _FP4[b & 0x0F]
-    vals[..., 1::2] = _FP4[b >> 4]
-    vals = torch.ldexp(vals, (scales.to(torch.int64) - 127).unsqueeze(-1).to(torch.float64))
+    # float32 is exact for every scale <= 254 (2**127 is representable and the
+    # product overflows to inf exactly when the reference's does); scale 255
+    # needs the wider type because 2**128 itself overflows float32.
+    wide = bool((scales == 255).any())
+    ft = torch.float64 if wide else torch.float32
+    lut = _FP4.to(ft)
+    vals = torch.empty(rows, groups, 32, dtype=ft)
+    vals[..., 0::2] = lut[b & 0x0F]
+    vals[..., 1::2] = lut[b >> 4]
+    vals = vals * torch.pow(2.0, (scales.to(torch.int64) - 127).unsqueeze(-1).to(ft))
     vals = vals.to(torch.float32).to(dtype)
     return vals.reshape(rows, groups * 32).t().contiguous()
 

@@ -1,0 +1,90 @@
+"""The C-ABI library loads, exports every symbol include/bs_moe.h declares, and
+rejects bad arguments before touching a device (no GPU needed)."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import REPO
+from blockstreamer_b200 import _lib
+
+HEADER = os.path.join(REPO, "include", "bs_moe.h")
+
+
+def declared_functions():
+    src = open(HEADER).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    return sorted(set(re.findall(r"\b(bs_[a-z0-9_]+)\s*\(", src)))
+
+
+def test_header_declares_expected_entry_points():
+    names = declared_functions()
+    for n in ("bs_dequant_mxfp4", "bs_router", "bs_dispatch", "bs_moe_gate_up", "bs_moe_down",
+              "bs_combine", "bs_mxfp4_matmul", "bs_moe_forward", "bs_last_error_string"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for n in declared_functions():
+        assert hasattr(lib, n), n
+        assert n in _lib.SIGNATURES, f"{n} has no ctypes signature"
+
+
+def test_version_and_error_string():
+    lib = _lib.load()
+    assert lib.bs_version() >= 1
+    assert isinstance(lib.bs_last_error_string(), bytes)
+
+
+def _err(lib):
+    return lib.bs_last_error_string().decode()
+
+
+def test_null_and_misaligned_pointers_are_rejected():
+    lib = _lib.load()
+    assert lib.bs_dequant_mxfp4(None, None, 1, 1, 1, 1, None, None) == _lib.BS_ERR_INVALID_ARGUMENT
+    assert "null" in _err(lib)
+    bad = ctypes.c_void_p(0x1001)
+    good = ctypes.c_void_p(0x1000)
+    assert lib.bs_dequant_mxfp4(bad, good, 1, 1, 1, 1, good, None) == _lib.BS_ERR_MISALIGNED
+    assert "aligned" in _err(lib)
+
+
+def test_bad_shapes_are_rejected():
+    lib = _lib.load()
+    p = ctypes.c_void_p(0x1000)
+    # contraction not a multiple of 32
+    st = lib.bs_moe_gate_up(p, p, 4, 4, 2, 48, 64, p, p, p, 0, 1.702, 7.0, p, 0, None)
+    assert st == _lib.BS_ERR_INVALID_ARGUMENT and "multiple of 32" in _err(lib)
+    # top_k larger than the expert count
+    st = lib.bs_router(p, 0, p, p, 1, 4, 64, 4, 8, None, p, p, 2, None)
+    assert st == _lib.BS_ERR_INVALID_ARGUMENT
+    # unknown dtype code
+    st = lib.bs_router(p, 7, p, p, 1, 4, 64, 8, 2, None, p, p, 2, None)
+    assert st == _lib.BS_ERR_INVALID_ARGUMENT
+
+
+def test_workspace_capacity_is_checked():
+    lib = _lib.load()
+    p = ctypes.c_void_p(0x1000)
+    need = lib.bs_dispatch_workspace_bytes(1024, 4, 128)
+    assert need > 0
+    st = lib.bs_dispatch(p, 2, 1024, 4, 128, None, 0, p, p, p, None, p, need - 1, None)
+    assert st == _lib.BS_ERR_CAPACITY
+
+
+def test_workspace_size_formula():
+    lib = _lib.load()
+    small = lib.bs_moe_workspace_bytes(64, 256, 256, 8, 2)
+    big = lib.bs_moe_workspace_bytes(8192, 2880, 2880, 128, 4)
+    assert 0 < small < big
+    # x_perm + h + y for T*k rows dominate
+    assert big >= 8192 * 4 * (2880 + 2880 + 2880) * 2
+
+
+def test_python_raises_valueerror_with_message():
+    with pytest.raises(ValueError, match="null pointer"):
+        _lib.call("bs_dequant_mxfp4", None, None, 1, 1, 1, 1, None, None)
