@@ -26,15 +26,19 @@ int tc_grouped_launch(int mode, const void* x, const int32_t* offsets, int64_t r
                       int64_t max_rows_per_expert, int64_t E, int64_t K, int64_t N,
                       const void* blocks, const void* scales, const void* bias, int bias_f32,
                       float alpha, float limit, void* out, cudaStream_t st);
+bool tc_supported(const void* scales, int64_t K, int64_t N);
 
 namespace {
 
 // Tokens per expert above which the tensor-core path wins over the GEMV.
 constexpr int64_t kGemvMaxRowsPerExpert = 16;
 
-int pick_algo(int algo, int64_t rows_total, int64_t E) {
+// AUTO: the GEMV at few tokens per expert; the tensor-core kernel otherwise,
+// when the scale rows can be bulk-copied (16-byte aligned runs).
+int pick_algo(int algo, int64_t rows_total, int64_t E, const void* scales, int64_t K, int64_t N) {
   if (algo != BS_ALGO_AUTO) return algo;
-  return (rows_total <= kGemvMaxRowsPerExpert * E) ? BS_ALGO_GEMV : BS_ALGO_TCGEN05;
+  if (rows_total <= kGemvMaxRowsPerExpert * E) return BS_ALGO_GEMV;
+  return tc_supported(scales, K, N) ? BS_ALGO_TCGEN05 : BS_ALGO_GEMV;
 }
 
 int check_expert_args(const char* fn, const void* x, const void* blocks, const void* scales,
@@ -63,7 +67,7 @@ int gate_up(const void* x, const int32_t* offsets, int64_t rows_total, int64_t m
   BS_ARG(I % 8 == 0, "bs_moe_gate_up: intermediate size must be a multiple of 8");
   if (rows_total == 0) return BS_OK;
   BS_TRY(check_device());
-  const int a = pick_algo(algo, rows_total, E);
+  const int a = pick_algo(algo, rows_total, E, scales, H, 2 * I);
   const int bf32 = bias_dtype == BS_F32;
   if (a == BS_ALGO_GEMV)
     return gemv_gate_up_launch(x, offsets, rows_total, E, H, I, blocks, scales, bias, bf32, alpha,
@@ -80,7 +84,7 @@ int down(const void* h, const int32_t* offsets, int64_t rows_total, int64_t max_
   BS_ARG(offsets, "bs_moe_down: null expert_offsets");
   if (rows_total == 0) return BS_OK;
   BS_TRY(check_device());
-  const int a = pick_algo(algo, rows_total, E);
+  const int a = pick_algo(algo, rows_total, E, scales, I, H);
   const int bf32 = bias_dtype == BS_F32;
   if (a == BS_ALGO_GEMV)
     return gemv_plain_launch(h, offsets, rows_total, E, I, H, blocks, scales, bias, bf32, y, st);
@@ -151,7 +155,7 @@ extern "C" int bs_mxfp4_matmul(const void* x, int64_t m, int64_t K, const void* 
   if (m == 0) return BS_OK;
   BS_TRY(check_device());
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const int a = pick_algo(algo, m, 1);
+  const int a = pick_algo(algo, m, 1, scales, K, N);
   if (a == BS_ALGO_GEMV)
     return gemv_plain_launch(x, nullptr, m, 1, K, N, blocks, scales, bias, 0, out, st);
   return tc_grouped_launch(1, x, nullptr, m, m, 1, K, N, blocks, scales, bias, 0, 0.f, 0.f, out, st);

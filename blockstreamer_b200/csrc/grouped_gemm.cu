@@ -8,16 +8,16 @@
 // to 320 TOKEN rows of one expert, so at uniform routing every weight byte is
 // fetched and dequantized once per layer.
 //   * A (weights): TMA brings the packed e2m1 bytes of a 128x64 slice into
-//     shared memory; four dequant warps decode them (bit-exact with the
-//     reference's LUT + ldexp) and write bf16 straight into TENSOR MEMORY with
-//     tcgen05.st — the MMA reads A from TMEM ("TS" form), so the dequantized
-//     weights never touch shared memory.
+//     shared memory and a bulk copy brings the tile's e8m0 scale rows; eight
+//     dequant warps (two groups taking alternate K steps) decode them bit-exactly
+//     and write bf16 straight into TENSOR MEMORY with tcgen05.st — the MMA reads
+//     A from TMEM ("TS" form), so dequantized weights never touch shared memory.
 //   * B (tokens): 128B-swizzled TMA tiles of 64 x 64 bf16 in shared memory.
 //   * D: fp32 accumulators in TMEM (up to 320 columns: one 128x256 and one
 //     128x64 MMA per K16 step), drained by four epilogue warps with tcgen05.ld.
-// Warp roles (320 threads): 0 TMA producer, 1 MMA issuer (+TMEM owner),
-// 2-5 epilogue, 6-9 dequant.  A 4-stage mbarrier pipeline links them; every
-// wait is bounded (timeout -> status word + clean exit, TMEM freed).
+// Warp roles (448 threads): 0 TMA producer, 1 MMA issuer (+TMEM owner),
+// 2-5 epilogue, 6-13 dequant.  mbarrier pipelines link them; every wait is
+// bounded (timeout -> status word + clean exit, TMEM freed).
 // MODE 0: gate_up — bias + clamped interleaved SwiGLU (gptoss.py:130-135,158-166).
 // MODE 1: plain   — bias (gptoss.py:167-174) / mxfp4_matmul.
 #include <cudaTypedefs.h>
@@ -28,20 +28,24 @@
 namespace bs {
 namespace {
 
-constexpr int kBM = 128;                      // weight rows per tile (MMA M)
-constexpr int kBK = 64;                       // K per pipeline stage
-constexpr int kNMax = 320;                    // token rows per tile
+constexpr int kBM = 128;                       // weight rows per tile (MMA M)
+constexpr int kBK = 64;                        // K per pipeline stage
+constexpr int kNMax = 320;                     // token rows per tile
 constexpr int kStages = 4;
-constexpr int kBoxRows = 64;                  // token rows per TMA box
+constexpr int kBoxRows = 64;                   // token rows per TMA box
 constexpr int kBoxBytes = kBoxRows * kBK * 2;  // 8 KiB
-constexpr int kBBytes = kNMax * kBK * 2;      // 40 KiB
-constexpr int kABytes = kBM * kBK / 2;        // 4 KiB of e2m1 bytes
+constexpr int kBBytes = kNMax * kBK * 2;       // 40 KiB
+constexpr int kABytes = kBM * kBK / 2;         // 4 KiB of e2m1 bytes
 constexpr int kStageBytes = kBBytes + kABytes;
-constexpr int kACol = 320;                    // TMEM column of the A ring
+constexpr int kMaxGroups = 128;                // K <= 4096
+constexpr int kScaleBufBytes = kBM * kMaxGroups;  // one tile's scale rows (16 KiB max)
+constexpr int kACol = 320;                     // TMEM column of the A ring
 constexpr int kTmemCols = 512;
-constexpr int kThreads = 320;
+constexpr int kDeqGroups = 2;
 constexpr int kWarpTMA = 0, kWarpMMA = 1, kWarpEpi0 = 2, kWarpDeq0 = 6;
-constexpr int kNumBars = 3 * kStages + 3;     // full, adone, empty per stage; accfull, accempty, drain
+constexpr int kThreads = (kWarpDeq0 + 4 * kDeqGroups) * 32;
+// barriers: full, adone, empty per stage; sfull, sempty per scale buffer; accfull, accempty, drain
+constexpr int kNumBars = 3 * kStages + 4 + 3;
 
 static_assert(kStageBytes % 1024 == 0, "stages must keep 1024-byte alignment for SW128");
 static_assert(kACol + kStages * (kBK / 2) <= kTmemCols, "TMEM budget");
@@ -100,13 +104,6 @@ __device__ __forceinline__ Tile decode_item(const int* off, const int* ipre, int
   return t;
 }
 
-__device__ __forceinline__ uint32_t load_scale_pair(const uint8_t* srow, int g0, int G, bool valid) {
-  uint32_t a = 127u, b = 127u;
-  if (valid && g0 < G) a = __ldg(srow + g0);
-  if (valid && g0 + 1 < G) b = __ldg(srow + g0 + 1);
-  return a | (b << 8);
-}
-
 __device__ __forceinline__ float bias_at(const void* bias, int f32, int64_t i) {
   if (!bias) return 0.f;
   return f32 ? static_cast<const float*>(bias)[i]
@@ -119,6 +116,14 @@ __device__ __forceinline__ bool warp_wait(uint32_t bar, uint32_t parity, volatil
   return __all_sync(0xffffffffu, ok);
 }
 
+// SwiGLU of the reference (gptoss.py:130-135) with the hardware exponential;
+// its few-ulp error is far below the bf16 rounding of the output.
+__device__ __forceinline__ float swiglu_fast(float gate, float up, float alpha, float limit) {
+  gate = fminf(gate, limit);
+  up = fminf(fmaxf(up, -limit), limit);
+  return (up + 1.0f) * __fdividef(gate, 1.0f + __expf(-alpha * gate));
+}
+
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1) tc_grouped_kernel(
     const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_a,
@@ -128,7 +133,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_kernel(
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint8_t* sbuf = smem + kStages * kStageBytes;  // [2][kScaleBufBytes]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sbuf + 2 * kScaleBufBytes);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   int* off = reinterpret_cast<int*>(tmem_holder + 2);
@@ -139,14 +145,20 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_kernel(
   auto full = [&](int s) { return bar(s); };
   auto adone = [&](int s) { return bar(kStages + s); };
   auto empty = [&](int s) { return bar(2 * kStages + s); };
-  const uint32_t accfull = bar(3 * kStages), accempty = bar(3 * kStages + 1),
-                 drain = bar(3 * kStages + 2);
+  auto sfull = [&](int b) { return bar(3 * kStages + b); };
+  auto sempty = [&](int b) { return bar(3 * kStages + 2 + b); };
+  const uint32_t accfull = bar(3 * kStages + 4), accempty = bar(3 * kStages + 5),
+                 drain = bar(3 * kStages + 6);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       ptx::mbar_init(full(s), 1);
       ptx::mbar_init(adone(s), 4);
       ptx::mbar_init(empty(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(sfull(b), 1);
+      ptx::mbar_init(sempty(b), 4 * kDeqGroups);
     }
     ptx::mbar_init(accfull, 1);
     ptx::mbar_init(accempty, 4);
@@ -177,12 +189,21 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_kernel(
     if (lane == 0) {
       int last_round[kStages];
       for (int s = 0; s < kStages; ++s) last_round[s] = -1;
-      uint32_t g = 0;
+      int last_srnd[2] = {-1, -1};
+      uint32_t g = 0, j = 0;
       bool ok = true;
-      for (int item = blockIdx.x; ok && item < total; item += gridDim.x) {
+      for (int item = blockIdx.x; ok && item < total; item += gridDim.x, ++j) {
         const Tile t = decode_item(off, ipre, E, MT, item);
         const int nbox = (t.nmma + kBoxRows - 1) / kBoxRows;
         const int arow = t.e * Nw + t.mt * kBM;
+        // the tile's scale rows: one contiguous run of valid_rows * G bytes
+        const int b = j & 1, sr = j >> 1;
+        if (!ptx::mbar_wait(sempty(b), (sr & 1) ^ 1, abort_flag)) { ok = false; break; }
+        const int vrows = min(kBM, Nw - t.mt * kBM);
+        ptx::mbar_arrive_expect_tx(sfull(b), (uint32_t)(vrows * G));
+        ptx::bulk_load(ptx::smem_addr(sbuf + b * kScaleBufBytes), scales + (int64_t)arow * G,
+                       (uint32_t)(vrows * G), sfull(b));
+        last_srnd[b] = sr;
         for (int ks = 0; ks < KS; ++ks, ++g) {
           const int s = g % kStages, r = g / kStages;
           if (!ptx::mbar_wait(empty(s), (r & 1) ^ 1, abort_flag)) { ok = false; break; }
@@ -198,6 +219,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_kernel(
       if (!ok) {  // let issued copies land before the CTA exits
         for (int s = 0; s < kStages; ++s)
           if (last_round[s] >= 0) ptx::mbar_wait(full(s), last_round[s] & 1, abort_flag, 200000000LL);
+        for (int b = 0; b < 2; ++b)
+          if (last_srnd[b] >= 0) ptx::mbar_wait(sfull(b), last_srnd[b] & 1, abort_flag, 200000000LL);
       }
     }
     __syncwarp();
@@ -246,6 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_kernel(
   } else if (warp < kWarpDeq0) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
+    const int odd = lane & 1;
     uint32_t j = 0;
     for (int item = blockIdx.x; item < total; item += gridDim.x, ++j) {
       const Tile t = decode_item(off, ipre, E, MT, item);
@@ -254,33 +278,38 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_kernel(
       const int row_w = t.mt * kBM + q * 32 + lane;
       const bool rv = row_w < Nw;
       const float bv = rv ? bias_at(bias, bias_f32, (int64_t)t.e * Nw + row_w) : 0.f;
+      const float bp = __shfl_xor_sync(0xffffffffu, bv, 1);
       const uint32_t taddr = tbase + ((uint32_t)(q * 32) << 16);
       for (int c0 = 0; c0 < t.nmma; c0 += 16) {
         uint32_t v[16];
         ptx::tmem_ld_32x32b_x16(taddr + c0, v);
         ptx::tmem_wait_ld();
         if (MODE == 0) {
-          const float bp = __shfl_xor_sync(0xffffffffu, bv, 1);
-          const int odd = lane & 1;
-          const int Iout = Nw / 2;
+          // Lane pair (2i, 2i+1) holds the gate and up rows of one output column.
+          // The even lane produces the pair's even token columns, the odd lane the
+          // odd ones; each sends its partner the value the partner lacks.
+          const int Iout = Nw >> 1;
+          uint16_t* orow = out + (row_w >> 1);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const uint32_t pv = __shfl_xor_sync(0xffffffffu, v[i], 1);
-            const int n = c0 + i;
-            if ((i & 1) == odd && n < t.nrows && rv) {
-              const float own = __uint_as_float(v[i]) + bv;
-              const float oth = __uint_as_float(pv) + bp;
-              const float hv = odd ? swiglu(oth, own, alpha, limit) : swiglu(own, oth, alpha, limit);
-              out[(t.r0 + n) * Iout + (row_w >> 1)] = __bfloat16_as_ushort(__float2bfloat16_rn(hv));
-            }
+          for (int jj = 0; jj < 8; ++jj) {
+            const uint32_t e0 = v[2 * jj], e1 = v[2 * jj + 1];
+            const uint32_t mine = odd ? e1 : e0;     // my row at my column
+            const uint32_t give = odd ? e0 : e1;     // my row at the partner's column
+            const uint32_t got = __shfl_xor_sync(0xffffffffu, give, 1);  // partner's row at my column
+            const float own = __uint_as_float(mine) + bv;
+            const float oth = __uint_as_float(got) + bp;
+            const float hv = odd ? swiglu_fast(oth, own, alpha, limit) : swiglu_fast(own, oth, alpha, limit);
+            const int n = c0 + 2 * jj + odd;
+            if (n < t.nrows && rv)
+              orow[(t.r0 + n) * Iout] = __bfloat16_as_ushort(__float2bfloat16_rn(hv));
           }
         } else {
+          uint16_t* ocol = out + row_w;
 #pragma unroll
           for (int i = 0; i < 16; ++i) {
             const int n = c0 + i;
             if (n < t.nrows && rv)
-              out[(t.r0 + n) * Nw + row_w] =
-                  __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[i]) + bv));
+              ocol[(t.r0 + n) * Nw] = __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[i]) + bv));
           }
         }
       }
@@ -290,28 +319,27 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_kernel(
     }
   } else {
     // ------------------------------------------------------------ dequant (A -> TMEM)
+    const int dg = (warp - kWarpDeq0) >> 2;  // dequant group: takes K steps ks = dg, dg+2, ...
     const int q = warp & 3;
-    const int r = q * 32 + lane;  // TMEM lane == row within the weight tile
+    const int r = q * 32 + lane;            // TMEM lane == row within the weight tile
     const uint32_t taddr = tbase + ((uint32_t)(q * 32) << 16) + kACol;
-    uint32_t g = 0;
+    uint32_t gbase = 0, j = 0;
     bool ok = true;
-    for (int item = blockIdx.x; ok && item < total; item += gridDim.x) {
-      const Tile t = decode_item(off, ipre, E, MT, item);
-      const int row_w = t.mt * kBM + r;
-      const bool rv = row_w < Nw;
-      const uint8_t* srow = scales + ((int64_t)t.e * Nw + (rv ? row_w : 0)) * G;
-      uint32_t sc_next = load_scale_pair(srow, 0, G, rv);
-      uint32_t sc_next2 = load_scale_pair(srow, 2, G, rv);
-      for (int ks = 0; ks < KS; ++ks, ++g) {
-        const uint32_t sc = sc_next;
-        sc_next = sc_next2;
-        sc_next2 = load_scale_pair(srow, 2 * (ks + 2), G, rv);
+    for (int item = blockIdx.x; ok && item < total; item += gridDim.x, ++j, gbase += KS) {
+      (void)decode_item(off, ipre, E, MT, item);
+      const int b = j & 1;
+      if (!warp_wait(sfull(b), (j >> 1) & 1, abort_flag)) { ok = false; break; }
+      const uint8_t* srow = sbuf + b * kScaleBufBytes + r * G;
+      for (int ks = dg; ks < KS; ks += kDeqGroups) {
+        const uint32_t g = gbase + ks;
         const int s = g % kStages;
         const uint32_t ph = (g / kStages) & 1;
+        const int g0 = 2 * ks;
+        const uint32_t s0 = srow[g0];
+        const uint32_t s1 = (g0 + 1 < G) ? srow[g0 + 1] : 127u;
         if (!warp_wait(full(s), ph, abort_flag)) { ok = false; break; }
         const uint4* src = reinterpret_cast<const uint4*>(smem + s * kStageBytes + kBBytes + r * 32);
         const uint4 b0 = src[0], b1 = src[1];
-        const uint32_t s0 = sc & 0xFFu, s1 = sc >> 8;
         const E2M1Pool p0 = make_e2m1_pool(s0), p1 = make_e2m1_pool(s1);
         uint32_t v[32];
         e2m1x8_decode(b0.x, s0, p0, v + 0);
@@ -328,6 +356,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_kernel(
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(adone(s));
       }
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(sempty(b));
     }
   }
 
@@ -370,6 +400,13 @@ int make_map_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64
 
 }  // namespace
 
+// Whether the tcgen05 path can take these weights: the per-tile scale rows are
+// bulk-copied, which needs 16-byte aligned, 16-byte multiple runs.
+bool tc_supported(const void* scales, int64_t K, int64_t N) {
+  const int64_t G = K / 32;
+  return (reinterpret_cast<uintptr_t>(scales) & 15) == 0 && (N * G) % 16 == 0 && G <= kMaxGroups;
+}
+
 int tc_grouped_launch(int mode, const void* x, const int32_t* offsets, int64_t rows_total,
                       int64_t max_rows_per_expert, int64_t E, int64_t K, int64_t N,
                       const void* blocks, const void* scales, const void* bias, int bias_f32,
@@ -379,13 +416,16 @@ int tc_grouped_launch(int mode, const void* x, const int32_t* offsets, int64_t r
          "tcgen05 GEMM: sizes exceed 32-bit TMA coordinates");
   BS_ARG(mode == 1 || N % 2 == 0, "tcgen05 GEMM: gate_up rows must be even");
   BS_ARG(offsets || E == 1, "tcgen05 GEMM: expert_offsets required");
+  BS_ARG(K / 32 <= kMaxGroups, "tcgen05 GEMM: contraction size above %d", kMaxGroups * 32);
+  BS_REQUIRE(tc_supported(scales, K, N), BS_ERR_MISALIGNED,
+             "tcgen05 GEMM: scales must be 16-byte aligned with rows*groups a multiple of 16");
   const int64_t G = K / 32;
   CUtensorMap tm_b, tm_a;
   BS_TRY(make_map_2d(&tm_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, x, (uint64_t)K, (uint64_t)rows_total,
                      (uint64_t)K * 2, kBK, kBoxRows, CU_TENSOR_MAP_SWIZZLE_128B));
   BS_TRY(make_map_2d(&tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, blocks, (uint64_t)G * 16, (uint64_t)(E * N),
                      (uint64_t)G * 16, kBK / 2, kBM, CU_TENSOR_MAP_SWIZZLE_NONE));
-  const size_t smem = 1024 + (size_t)kStages * kStageBytes + kNumBars * 8 + 16 +
+  const size_t smem = 1024 + (size_t)kStages * kStageBytes + 2 * kScaleBufBytes + kNumBars * 8 + 16 +
                       (size_t)2 * (E + 1) * sizeof(int);
   BS_REQUIRE(smem <= 227 * 1024, BS_ERR_CAPACITY, "tcgen05 GEMM: too many experts for shared memory");
   auto kern = mode == 0 ? tc_grouped_kernel<0> : tc_grouped_kernel<1>;
