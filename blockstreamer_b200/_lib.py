@@ -37,6 +37,7 @@ SIGNATURES = {
     "bs_router": (_i32, [_vp, _i32, _vp, _vp, _i32, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _i32, _vp]),
     "bs_dispatch_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "bs_dispatch": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
+    "bs_dispatch_noalloc": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _vp]),
     "bs_moe_gate_up": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _i32, _f32,
                               _f32, _vp, _i32, _vp]),
     "bs_moe_down": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _i32, _vp, _i32, _vp]),

@@ -10,6 +10,8 @@
 //               __match_any_sync / __popc, warps and blocks are ordered by scans,
 //               so rows of an expert keep (token, slot) order (deterministic);
 //   4. gather   x_perm[row] = x[token_of_row[row]] with 16-byte copies.
+#include <mutex>
+
 #include "bs_common.cuh"
 
 namespace bs {
@@ -249,4 +251,69 @@ extern "C" int bs_dispatch(const void* indices, int index_dtype, int64_t T, int6
   return bs::dispatch_launch(indices, index_dtype, T, k, E, x, H, expert_offsets, row_of_slot,
                              token_of_row, x_perm, workspace, workspace_bytes,
                              reinterpret_cast<cudaStream_t>(stream));
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free dispatch (bs_dispatch_noalloc).
+//
+// Some callers cannot allocate device memory at the point where they dispatch
+// tokens: code running while a CUDA graph is being captured (cudaMalloc is not
+// permitted inside a capture), serving loops that must not stall on the device
+// synchronization cudaMalloc/cudaFree imply, runtimes that pre-reserve all
+// device memory in their own pools, and foreign-language callers (ctypes, cgo,
+// JNI) that have no allocator to hand a workspace from.  For them this entry
+// point keeps its scratch (the per-block expert counts and their prefix) in a
+// fixed device array owned by the library, so the caller passes only inputs
+// and outputs.
+namespace bs {
+namespace {
+
+// Scratch limit: 2 * ceil(T/256) * E ints <= 512 KiB, e.g. T <= 65536 tokens
+// with E <= 256 experts.  Every GPU that loads this library holds this array
+// until the process exits.
+constexpr size_t kNoAllocScratchBytes = 512 * 1024;
+static __device__ __align__(256) int g_dispatch_scratch[kNoAllocScratchBytes / sizeof(int)];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {};
+
+// Device address of the scratch array on the current device.  The array's name
+// is only a host-side handle, so the address is looked up once per device, with
+// that device current, on the first call made on it.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  BS_CUDA(cudaGetDevice(&dev));
+  BS_REQUIRE(dev >= 0 && dev < 64, BS_ERR_UNSUPPORTED, "bs_dispatch_noalloc: device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    BS_CUDA(cudaGetSymbolAddress(&p, g_dispatch_scratch));
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return BS_OK;
+}
+
+}  // namespace
+}  // namespace bs
+
+extern "C" int bs_dispatch_noalloc(const void* indices, int index_dtype, int64_t T, int64_t k,
+                                   int64_t E, const void* x, int64_t H, int32_t* expert_offsets,
+                                   int32_t* row_of_slot, int32_t* token_of_row, void* x_perm,
+                                   void* stream) {
+  using namespace bs;
+  BS_ARG(T >= 0 && k > 0 && E > 0, "bs_dispatch_noalloc: bad sizes");
+  const size_t need = dispatch_workspace_bytes(T, k, E);
+  BS_REQUIRE(need <= kNoAllocScratchBytes, BS_ERR_CAPACITY,
+             "bs_dispatch_noalloc: T=%lld, E=%lld needs %zu bytes of scratch, above the fixed %zu "
+             "(2 * ceil(T/256) * E * 4 bytes must fit; use bs_dispatch with a workspace)",
+             (long long)T, (long long)E, need, kNoAllocScratchBytes);
+  BS_TRY(check_device());
+  void* scratch = nullptr;
+  BS_TRY(noalloc_scratch(&scratch));
+  // The scratch is fully rewritten by every call (counts, then prefixes), so
+  // nothing has to start at zero.
+  return dispatch_launch(indices, index_dtype, T, k, E, x, H, expert_offsets, row_of_slot,
+                         token_of_row, x_perm, scratch, kNoAllocScratchBytes,
+                         reinterpret_cast<cudaStream_t>(stream));
 }

@@ -96,6 +96,24 @@ int bs_dispatch(const void* indices, int index_dtype, int64_t T, int64_t k, int6
                 int32_t* token_of_row, void* x_perm, void* workspace, size_t workspace_bytes,
                 void* stream);
 
+/* Allocation-free dispatch: the same outputs as bs_dispatch, with its scratch
+ * held in a fixed 512 KiB device array inside the library instead of a caller
+ * workspace.  No counterpart in the reference (its dispatch is Python that
+ * allocates freely).  It serves callers that cannot allocate device memory
+ * where they dispatch: code inside a CUDA graph capture, serving loops that
+ * must not stall on cudaMalloc/cudaFree, runtimes whose pools own all device
+ * memory, and ctypes/cgo/JNI callers without a device allocator.
+ * Limits: 2 * ceil(T/256) * E * 4 bytes <= 512 KiB (e.g. T <= 65536 tokens
+ * with E <= 256), else BS_ERR_CAPACITY.  It allocates nothing; the first call
+ * on each device looks up the array's device address (make that first call
+ * before any stream capture).  Every call on a device shares the one array:
+ * calls whose kernels overlap on the GPU (different streams without ordering)
+ * race and give wrong results; the array keeps the last call's contents, which
+ * every call fully rewrites before reading. */
+int bs_dispatch_noalloc(const void* indices, int index_dtype, int64_t T, int64_t k, int64_t E,
+                        const void* x, int64_t H, int32_t* expert_offsets, int32_t* row_of_slot,
+                        int32_t* token_of_row, void* x_perm, void* stream);
+
 /* Grouped gate_up projection + bias + clamped, interleaved SwiGLU.
  * Replaces block_streamer/gptoss.py:158-166 with _apply_gate (130-135):
  *   g = x_perm[rows of e] @ dequant(W_gu[e]) + b_gu[e]        (fp32 accumulate)
