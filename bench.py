@@ -198,34 +198,52 @@ def run_reference(args, rank, world):
 # ---------------------------------------------------------------- our arm
 
 STAGES = ("router", "dispatch", "gate_up", "down", "combine")
-LAUNCHES = {"router": 1, "dispatch": 4, "gate_up": 1, "down": 1, "combine": 1}
+LAUNCHES = {"router": 3, "dispatch": 4, "gate_up": 1, "down": 1, "combine": 1}
 
 
 def layer_stages(x, p, k, algo, bufs):
-    """The layer as its C-ABI stages (the same kernels bs_moe_forward runs)."""
+    """The layer as its C-ABI stages (the same kernels bs_moe_forward runs),
+    with every output and workspace allocated once up front."""
+    dev = x.device
     E = p["experts.gate_up_proj_blocks"].shape[0]
-    T = x.shape[0]
+    T, H = x.shape
+    I = p["experts.gate_up_proj_blocks"].shape[1] // 2
+    S = T * k
+    lib = kernels._lib.load()
+    bufs["sc"] = torch.empty(T, k, dtype=torch.float32, device=dev)
+    bufs["idx"] = torch.empty(T, k, dtype=torch.int32, device=dev)
+    bufs["rws"] = torch.empty(lib.bs_router_workspace_bytes(T, H, E, kernels._lib.BS_F32),
+                              dtype=torch.uint8, device=dev)
+    bufs["d"] = kernels.Dispatch(torch.empty(E + 1, dtype=torch.int32, device=dev),
+                                 torch.empty(S, dtype=torch.int32, device=dev),
+                                 torch.empty(S, dtype=torch.int32, device=dev),
+                                 torch.empty(S, H, dtype=torch.bfloat16, device=dev))
+    bufs["dws"] = torch.empty(lib.bs_dispatch_workspace_bytes(T, k, E), dtype=torch.uint8, device=dev)
+    bufs["h"] = torch.empty(S, I, dtype=torch.bfloat16, device=dev)
+    bufs["y"] = torch.empty(S, H, dtype=torch.bfloat16, device=dev)
+    bufs["out"] = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
 
     def router():
-        _, bufs["sc"], bufs["idx"] = kernels.router(x, p["router.weight"], p["router.bias"], k,
-                                                    index_dtype=torch.int32, return_logits=T <= 8)
+        kernels.router(x, p["router.weight"], p["router.bias"], k, out_scores=bufs["sc"],
+                       out_indices=bufs["idx"], workspace=bufs["rws"])
 
     def dispatch():
-        bufs["d"] = kernels.dispatch(bufs["idx"], E, x)
+        kernels.dispatch(bufs["idx"], E, x, out=bufs["d"], workspace=bufs["dws"])
 
     def gate_up():
         d = bufs["d"]
-        bufs["h"] = kernels.moe_gate_up(d.x_perm, d.expert_offsets, p["experts.gate_up_proj_blocks"],
-                                        p["experts.gate_up_proj_scales"], p["experts.gate_up_proj_bias"],
-                                        algo=algo)
+        kernels.moe_gate_up(d.x_perm, d.expert_offsets, p["experts.gate_up_proj_blocks"],
+                            p["experts.gate_up_proj_scales"], p["experts.gate_up_proj_bias"],
+                            algo=algo, out=bufs["h"])
 
     def down():
         d = bufs["d"]
-        bufs["y"] = kernels.moe_down(bufs["h"], d.expert_offsets, p["experts.down_proj_blocks"],
-                                     p["experts.down_proj_scales"], p["experts.down_proj_bias"], algo=algo)
+        kernels.moe_down(bufs["h"], d.expert_offsets, p["experts.down_proj_blocks"],
+                         p["experts.down_proj_scales"], p["experts.down_proj_bias"], algo=algo,
+                         out=bufs["y"])
 
     def combine():
-        bufs["out"] = kernels.combine(bufs["y"], bufs["d"].row_of_slot, bufs["sc"], T)
+        kernels.combine(bufs["y"], bufs["d"].row_of_slot, bufs["sc"], T, out=bufs["out"])
 
     return {"router": router, "dispatch": dispatch, "gate_up": gate_up, "down": down, "combine": combine}
 

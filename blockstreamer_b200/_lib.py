@@ -34,7 +34,9 @@ SIGNATURES = {
     "bs_last_error_string": (_c.c_char_p, []),
     "bs_device_status": (_i32, [_c.POINTER(_c.c_int), _i32, _vp]),
     "bs_dequant_mxfp4": (_i32, [_vp, _vp, _i64, _i64, _i64, _i32, _vp, _vp]),
-    "bs_router": (_i32, [_vp, _i32, _vp, _vp, _i32, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _i32, _vp]),
+    "bs_router_workspace_bytes": (_sz, [_i64, _i64, _i64, _i32]),
+    "bs_router": (_i32, [_vp, _i32, _vp, _vp, _i32, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _i32, _vp,
+                         _sz, _vp]),
     "bs_dispatch_workspace_bytes": (_sz, [_i64, _i64, _i64]),
     "bs_dispatch": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _sz, _vp]),
     "bs_dispatch_noalloc": (_i32, [_vp, _i32, _i64, _i64, _i64, _vp, _i64, _vp, _vp, _vp, _vp, _vp]),

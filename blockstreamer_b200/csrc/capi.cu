@@ -6,7 +6,8 @@ namespace bs {
 
 int router_launch(const void* x, int x_dtype, const void* weight, const void* bias, int w_dtype,
                   int64_t T, int64_t H, int64_t E, int64_t k, float* logits, float* scores,
-                  void* indices, int index_dtype, cudaStream_t st);
+                  void* indices, int index_dtype, void* ws, size_t ws_bytes, cudaStream_t st);
+size_t router_workspace_bytes(int64_t T, int64_t H, int64_t E, int w_dtype);
 size_t dispatch_workspace_bytes(int64_t T, int64_t k, int64_t E);
 int dispatch_launch(const void* indices, int index_dtype, int64_t T, int64_t k, int64_t E,
                     const void* x, int64_t H, int32_t* offsets, int32_t* row_of_slot,
@@ -93,7 +94,8 @@ int down(const void* h, const int32_t* offsets, int64_t rows_total, int64_t max_
 }
 
 struct Workspace {
-  float* logits;
+  void* router;
+  size_t router_bytes;
   void* dispatch;
   size_t dispatch_bytes;
   int32_t* offsets;
@@ -114,7 +116,9 @@ Workspace carve(void* base, int64_t T, int64_t H, int64_t I, int64_t E, int64_t 
     return base ? static_cast<char*>(base) + at : nullptr;
   };
   const int64_t S = T * k;
-  w.logits = reinterpret_cast<float*>(take((size_t)T * E * sizeof(float)));
+  // sized for an fp32 router (the larger split); a bf16 router uses less
+  w.router_bytes = router_workspace_bytes(T, H, E, BS_F32);
+  w.router = take(w.router_bytes);
   w.dispatch_bytes = dispatch_workspace_bytes(T, k, E);
   w.dispatch = take(w.dispatch_bytes);
   w.offsets = reinterpret_cast<int32_t*>(take((size_t)(E + 1) * sizeof(int32_t)));
@@ -187,8 +191,8 @@ extern "C" int bs_moe_forward(const void* x, int64_t T, int64_t H, int64_t I, in
   BS_ALIGNED16(workspace, "workspace");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (router_weight)
-    BS_TRY(router_launch(x, BS_BF16, router_weight, router_bias, router_dtype, T, H, E, k, w.logits,
-                         scores, indices, BS_I32, st));
+    BS_TRY(router_launch(x, BS_BF16, router_weight, router_bias, router_dtype, T, H, E, k, nullptr,
+                         scores, indices, BS_I32, w.router, w.router_bytes, st));
   BS_TRY(dispatch_launch(indices, BS_I32, T, k, E, x, H, w.offsets, w.row_of_slot, w.token_of_row,
                          w.x_perm, w.dispatch, w.dispatch_bytes, st));
   const int64_t S = T * k;

@@ -370,34 +370,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_kernel(
   }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
-  return fn;
-}
-
-int make_map_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t inner,
-                uint64_t outer, uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
-                CUtensorMapSwizzle sw) {
-  auto fn = encode_fn();
-  BS_REQUIRE(fn, BS_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
-  cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {row_bytes};
-  cuuint32_t box[2] = {box_inner, box_outer};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  BS_REQUIRE(r == CUDA_SUCCESS, BS_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
-  return BS_OK;
-}
-
 }  // namespace
 
 // Whether the tcgen05 path can take these weights: the per-tile scale rows are

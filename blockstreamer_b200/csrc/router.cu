@@ -178,6 +178,27 @@ __global__ void __launch_bounds__(256) router_topk_kernel(const float* __restric
                     idx32 ? idx32 + (int64_t)t * k : nullptr, idx64 ? idx64 + (int64_t)t * k : nullptr);
 }
 
+// Sum the K-split partial logits of the tensor-core form, add the bias, then
+// top-k + softmax with one warp per token.
+__global__ void __launch_bounds__(256) router_finish_kernel(
+    const float* __restrict__ partial, int ns, int T, int Ep, int E, const void* __restrict__ bias,
+    int bias_f32, int bf16_logits, int k, float* __restrict__ logits, float* __restrict__ scores,
+    int32_t* __restrict__ idx32, int64_t* __restrict__ idx64) {
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  if (t >= T) return;
+  auto get = [&](int e) {
+    float v = 0.f;
+    for (int s = 0; s < ns; ++s) v += partial[((int64_t)s * T + t) * Ep + e];
+    v += bias_f32 ? static_cast<const float*>(bias)[e]
+                  : __bfloat162float(static_cast<const __nv_bfloat16*>(bias)[e]);
+    v = round_logit(v, bf16_logits);
+    if (logits) logits[(int64_t)t * E + e] = v;
+    return v;
+  };
+  warp_topk_softmax(get, E, k, scores + (int64_t)t * k, idx32 ? idx32 + (int64_t)t * k : nullptr,
+                    idx64 ? idx64 + (int64_t)t * k : nullptr);
+}
+
 template <typename XT, typename WT>
 int launch_router(const void* x, const void* w, const void* b, int T, int H, int E, int k,
                   bool bf16_logits, float* logits, float* scores, int32_t* i32, int64_t* i64,
@@ -205,9 +226,34 @@ int launch_router(const void* x, const void* w, const void* b, int T, int H, int
 
 }  // namespace
 
+int router_finish_launch(const float* partial, int ns, int64_t T, int64_t Ep, int64_t E,
+                         const void* bias, int bias_f32, int bf16_logits, int64_t k,
+                         float* logits, float* scores, void* indices, int index_dtype,
+                         cudaStream_t st) {
+  int32_t* i32 = index_dtype == BS_I32 ? static_cast<int32_t*>(indices) : nullptr;
+  int64_t* i64 = index_dtype == BS_I64 ? static_cast<int64_t*>(indices) : nullptr;
+  router_finish_kernel<<<(unsigned)cdiv(T, 8), 256, 0, st>>>(partial, ns, (int)T, (int)Ep, (int)E,
+                                                              bias, bias_f32, bf16_logits, (int)k,
+                                                              logits, scores, i32, i64);
+  BS_LAUNCHED();
+  return BS_OK;
+}
+
+size_t router_tc_workspace_bytes(int64_t T, int64_t H, int64_t E, int w_dtype);
+bool router_tc_supported(int x_dtype, int64_t T, int64_t H, int64_t E, int64_t k, const void* x);
+int router_tc_launch(const void* x, const void* weight, const void* bias, int w_dtype, int64_t T,
+                     int64_t H, int64_t E, int64_t k, float* logits, float* scores, void* indices,
+                     int index_dtype, void* ws, size_t ws_bytes, cudaStream_t st);
+
+// Workspace: the tensor-core form's split weight, and logits scratch for the
+// small-T form.
+size_t router_workspace_bytes(int64_t T, int64_t H, int64_t E, int w_dtype) {
+  return router_tc_workspace_bytes(T, H, E, w_dtype) + align_up((size_t)std::max<int64_t>(T, 1) * E * 4, 256);
+}
+
 int router_launch(const void* x, int x_dtype, const void* weight, const void* bias, int w_dtype,
                   int64_t T, int64_t H, int64_t E, int64_t k, float* logits, float* scores,
-                  void* indices, int index_dtype, cudaStream_t st) {
+                  void* indices, int index_dtype, void* ws, size_t ws_bytes, cudaStream_t st) {
   BS_ARG(x && weight && bias && scores && indices, "bs_router: null pointer");
   BS_ARG(x_dtype == BS_BF16 || x_dtype == BS_F32, "bs_router: x dtype must be bf16 or f32");
   BS_ARG(w_dtype == BS_BF16 || w_dtype == BS_F32, "bs_router: weight dtype must be bf16 or f32");
@@ -218,24 +264,38 @@ int router_launch(const void* x, int x_dtype, const void* weight, const void* bi
   BS_ARG(T <= (int64_t)INT32_MAX / 32 && H <= INT32_MAX, "bs_router: too many tokens");
   if (T == 0) return BS_OK;
   BS_TRY(check_device());
+  const size_t tc_bytes = router_tc_workspace_bytes(T, H, E, w_dtype);
+  if (ws && ws_bytes >= tc_bytes && router_tc_supported(x_dtype, T, H, E, k, x))
+    return router_tc_launch(x, weight, bias, w_dtype, T, H, E, k, logits, scores, indices,
+                            index_dtype, ws, ws_bytes, st);
+  // the small-T form needs a logits buffer: the caller's, or the workspace's
+  float* lg = logits;
+  if (!lg && ws && ws_bytes >= router_workspace_bytes(T, H, E, w_dtype))
+    lg = reinterpret_cast<float*>(static_cast<char*>(ws) + tc_bytes);
   int32_t* i32 = index_dtype == BS_I32 ? static_cast<int32_t*>(indices) : nullptr;
   int64_t* i64 = index_dtype == BS_I64 ? static_cast<int64_t*>(indices) : nullptr;
   const bool bl = w_dtype == BS_BF16;
   const int Ti = (int)T, Hi = (int)H, Ei = (int)E, ki = (int)k;
   if (x_dtype == BS_BF16 && w_dtype == BS_F32)
-    return launch_router<__nv_bfloat16, float>(x, weight, bias, Ti, Hi, Ei, ki, bl, logits, scores, i32, i64, st);
+    return launch_router<__nv_bfloat16, float>(x, weight, bias, Ti, Hi, Ei, ki, bl, lg, scores, i32, i64, st);
   if (x_dtype == BS_BF16 && w_dtype == BS_BF16)
-    return launch_router<__nv_bfloat16, __nv_bfloat16>(x, weight, bias, Ti, Hi, Ei, ki, bl, logits, scores, i32, i64, st);
+    return launch_router<__nv_bfloat16, __nv_bfloat16>(x, weight, bias, Ti, Hi, Ei, ki, bl, lg, scores, i32, i64, st);
   if (x_dtype == BS_F32 && w_dtype == BS_F32)
-    return launch_router<float, float>(x, weight, bias, Ti, Hi, Ei, ki, bl, logits, scores, i32, i64, st);
-  return launch_router<float, __nv_bfloat16>(x, weight, bias, Ti, Hi, Ei, ki, bl, logits, scores, i32, i64, st);
+    return launch_router<float, float>(x, weight, bias, Ti, Hi, Ei, ki, bl, lg, scores, i32, i64, st);
+  return launch_router<float, __nv_bfloat16>(x, weight, bias, Ti, Hi, Ei, ki, bl, lg, scores, i32, i64, st);
 }
 
 }  // namespace bs
 
+extern "C" size_t bs_router_workspace_bytes(int64_t T, int64_t H, int64_t E, int w_dtype) {
+  return bs::router_workspace_bytes(T, H, E, w_dtype);
+}
+
 extern "C" int bs_router(const void* x, int x_dtype, const void* weight, const void* bias,
                          int w_dtype, int64_t T, int64_t H, int64_t E, int64_t k, float* logits,
-                         float* scores, void* indices, int index_dtype, void* stream) {
+                         float* scores, void* indices, int index_dtype, void* workspace,
+                         size_t workspace_bytes, void* stream) {
   return bs::router_launch(x, x_dtype, weight, bias, w_dtype, T, H, E, k, logits, scores, indices,
-                           index_dtype, reinterpret_cast<cudaStream_t>(stream));
+                           index_dtype, workspace, workspace_bytes,
+                           reinterpret_cast<cudaStream_t>(stream));
 }

@@ -80,8 +80,15 @@ def dequant_mxfp4(blocks: torch.Tensor, scales: torch.Tensor, transpose: bool = 
 
 
 def router(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, top_k: int,
-           return_logits: bool = False, index_dtype: torch.dtype = torch.int64):
-    """GptOssTopKRouter.forward: returns (logits | None, scores [T,k] f32, indices [T,k])."""
+           return_logits: bool = False, index_dtype: torch.dtype = torch.int64,
+           use_workspace: bool = True, out_scores: torch.Tensor | None = None,
+           out_indices: torch.Tensor | None = None, workspace: torch.Tensor | None = None):
+    """GptOssTopKRouter.forward: returns (logits | None, scores [T,k] f32, indices [T,k]).
+
+    With ``use_workspace`` (default) the library may use its tensor-core form;
+    without, the fp32 CUDA-core form runs.  ``out_*`` and ``workspace`` let a
+    caller reuse buffers across calls.
+    """
     _cuda("router", x, weight, bias)
     T, H = x.shape
     E = weight.shape[0]
@@ -91,13 +98,21 @@ def router(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor, top_k: int
         raise ValueError("router weight and bias must share a dtype")
     x, weight, bias = _contig("x", x), _contig("weight", weight), _contig("bias", bias)
     dev = x.device
-    logits = torch.empty(T, E, dtype=torch.float32, device=dev) if (return_logits or T <= 8) else None
-    scores = torch.empty(T, top_k, dtype=torch.float32, device=dev)
-    idx = torch.empty(T, top_k, dtype=index_dtype, device=dev)
+    logits = torch.empty(T, E, dtype=torch.float32, device=dev) if return_logits else None
+    scores = out_scores if out_scores is not None else torch.empty(T, top_k, dtype=torch.float32, device=dev)
+    idx = out_indices if out_indices is not None else torch.empty(T, top_k, dtype=index_dtype, device=dev)
+    index_dtype = idx.dtype
+    ws, ws_bytes = None, 0
+    if use_workspace:
+        ws_bytes = _lib.load().bs_router_workspace_bytes(T, H, E, _DT[weight.dtype])
+        ws = workspace if workspace is not None and workspace.numel() >= ws_bytes else \
+            torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        ws_bytes = ws.numel()
     with torch.cuda.device(dev):
         _lib.call("bs_router", _p(x), _DT[x.dtype], _p(weight), _p(bias), _DT[weight.dtype],
-                  T, H, E, top_k, _p(logits), _p(scores), _p(idx), _DT[index_dtype], _stream(x))
-    return (logits if return_logits else None), scores, idx
+                  T, H, E, top_k, _p(logits), _p(scores), _p(idx), _DT[index_dtype], _p(ws), ws_bytes,
+                  _stream(x))
+    return logits, scores, idx
 
 
 @dataclass
@@ -108,25 +123,36 @@ class Dispatch:
     x_perm: torch.Tensor | None    # [T*k, H] bf16
 
 
-def dispatch(indices: torch.Tensor, num_experts: int, x: torch.Tensor | None = None) -> Dispatch:
-    """Group the (token, slot) pairs by expert; optionally gather x rows."""
+def dispatch(indices: torch.Tensor, num_experts: int, x: torch.Tensor | None = None,
+             out: Dispatch | None = None, workspace: torch.Tensor | None = None) -> Dispatch:
+    """Group the (token, slot) pairs by expert; optionally gather x rows.
+    ``out`` (a previous result of the same shapes) and ``workspace`` are reused when given."""
     _cuda("dispatch", indices, x)
     T, k = indices.shape
     indices = _contig("indices", indices)
     dev = indices.device
     S = T * k
-    offsets = torch.empty(num_experts + 1, dtype=torch.int32, device=dev)
-    row_of_slot = torch.empty(S, dtype=torch.int32, device=dev)
-    token_of_row = torch.empty(S, dtype=torch.int32, device=dev)
-    x_perm = None
+    if out is not None:
+        offsets, row_of_slot, token_of_row, x_perm = (out.expert_offsets, out.row_of_slot,
+                                                      out.token_of_row, out.x_perm)
+    else:
+        offsets = torch.empty(num_experts + 1, dtype=torch.int32, device=dev)
+        row_of_slot = torch.empty(S, dtype=torch.int32, device=dev)
+        token_of_row = torch.empty(S, dtype=torch.int32, device=dev)
+        x_perm = None
     H = 0
     if x is not None:
         x = _contig("x", x)
         H = x.shape[1]
-        x_perm = torch.empty(S, H, dtype=x.dtype, device=dev)
+        if x_perm is None:
+            x_perm = torch.empty(S, H, dtype=x.dtype, device=dev)
+    else:
+        x_perm = None
     lib = _lib.load()
     ws_bytes = lib.bs_dispatch_workspace_bytes(T, k, num_experts)
-    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    ws = workspace if workspace is not None and workspace.numel() >= ws_bytes else \
+        torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=dev)
+    ws_bytes = ws.numel()
     with torch.cuda.device(dev):
         _lib.call("bs_dispatch", _p(indices), _DT[indices.dtype], T, k, num_experts, _p(x), H,
                   _p(offsets), _p(row_of_slot), _p(token_of_row), _p(x_perm), _p(ws), ws_bytes,
@@ -143,7 +169,7 @@ def _bias_code(bias: torch.Tensor | None) -> int:
 
 
 def moe_gate_up(x_perm, expert_offsets, blocks, scales, bias, alpha=ALPHA, limit=LIMIT,
-                algo=ALGO_AUTO, max_rows_per_expert=None) -> torch.Tensor:
+                algo=ALGO_AUTO, max_rows_per_expert=None, out: torch.Tensor | None = None) -> torch.Tensor:
     """h [rows, I] = SwiGLU(x_perm @ dequant(W_gu[e]) + b_gu[e]) per expert segment."""
     _cuda("moe_gate_up", x_perm, expert_offsets, blocks, scales, bias)
     S, H = x_perm.shape
@@ -151,7 +177,7 @@ def moe_gate_up(x_perm, expert_offsets, blocks, scales, bias, alpha=ALPHA, limit
     if G * 32 != H or two_i % 2:
         raise ValueError(f"gate_up blocks {tuple(blocks.shape)} do not match hidden size {H}")
     I = two_i // 2
-    h = torch.empty(S, I, dtype=torch.bfloat16, device=x_perm.device)
+    h = out if out is not None else torch.empty(S, I, dtype=torch.bfloat16, device=x_perm.device)
     mr = S if max_rows_per_expert is None else max_rows_per_expert
     with torch.cuda.device(x_perm.device):
         _lib.call("bs_moe_gate_up", _p(x_perm), _p(expert_offsets), S, mr, E, H, I, _p(blocks),
@@ -160,14 +186,15 @@ def moe_gate_up(x_perm, expert_offsets, blocks, scales, bias, alpha=ALPHA, limit
     return h
 
 
-def moe_down(h, expert_offsets, blocks, scales, bias, algo=ALGO_AUTO, max_rows_per_expert=None) -> torch.Tensor:
+def moe_down(h, expert_offsets, blocks, scales, bias, algo=ALGO_AUTO, max_rows_per_expert=None,
+             out: torch.Tensor | None = None) -> torch.Tensor:
     """y [rows, H] = h @ dequant(W_d[e]) + b_d[e] per expert segment."""
     _cuda("moe_down", h, expert_offsets, blocks, scales, bias)
     S, I = h.shape
     E, H, G, _ = blocks.shape
     if G * 32 != I:
         raise ValueError(f"down blocks {tuple(blocks.shape)} do not match intermediate size {I}")
-    y = torch.empty(S, H, dtype=torch.bfloat16, device=h.device)
+    y = out if out is not None else torch.empty(S, H, dtype=torch.bfloat16, device=h.device)
     mr = S if max_rows_per_expert is None else max_rows_per_expert
     with torch.cuda.device(h.device):
         _lib.call("bs_moe_down", _p(h), _p(expert_offsets), S, mr, E, H, I, _p(blocks), _p(scales),
@@ -175,13 +202,14 @@ def moe_down(h, expert_offsets, blocks, scales, bias, algo=ALGO_AUTO, max_rows_p
     return y
 
 
-def combine(y: torch.Tensor, row_of_slot: torch.Tensor, weights: torch.Tensor, num_tokens: int) -> torch.Tensor:
+def combine(y: torch.Tensor, row_of_slot: torch.Tensor, weights: torch.Tensor, num_tokens: int,
+            out: torch.Tensor | None = None) -> torch.Tensor:
     """out[t] = sum_s weights[t,s] * y[row_of_slot[t*k+s]] (fp32 sum, bf16 out)."""
     _cuda("combine", y, row_of_slot, weights)
     k = row_of_slot.numel() // max(num_tokens, 1)
     H = y.shape[1]
     w = weights.float().contiguous()
-    out = torch.empty(num_tokens, H, dtype=torch.bfloat16, device=y.device)
+    out = out if out is not None else torch.empty(num_tokens, H, dtype=torch.bfloat16, device=y.device)
     with torch.cuda.device(y.device):
         _lib.call("bs_combine", _p(y), _p(row_of_slot), _p(w), num_tokens, k, H, _p(out), _stream(y))
     return out

@@ -74,11 +74,18 @@ int bs_dequant_mxfp4(const void* blocks, const void* scales, int64_t experts, in
  * Replaces transformers models/gpt_oss/modeling_gpt_oss.py:126-130
  * (GptOssTopKRouter.forward).  x [T,H] bf16 or f32 (x_dtype); weight [E,H] and
  * bias [E] f32 or bf16 (w_dtype; bf16 logits are rounded to bf16 before top-k,
- * as the reference computes them in the weight dtype).  Accumulation is fp32.
- * logits [T,E] f32 (may be NULL); scores [T,k] f32; indices [T,k] int32/int64. */
+ * as the reference computes them in the weight dtype).  Accumulation is fp32:
+ * with a workspace, bf16 x and T > 64 the logits come from the tensor cores
+ * with the fp32 weight split exactly into three bf16 terms; otherwise from fp32
+ * CUDA-core FMAs.  Top-k ties go to the lower expert index.
+ * logits [T,E] f32 (may be NULL); scores [T,k] f32; indices [T,k] int32/int64.
+ * workspace: bs_router_workspace_bytes(T, H, E, w_dtype) bytes (may be NULL:
+ * then the CUDA-core form runs). */
+size_t bs_router_workspace_bytes(int64_t T, int64_t H, int64_t E, int w_dtype);
 int bs_router(const void* x, int x_dtype, const void* weight, const void* bias, int w_dtype,
               int64_t T, int64_t H, int64_t E, int64_t k, float* logits, float* scores,
-              void* indices, int index_dtype, void* stream);
+              void* indices, int index_dtype, void* workspace, size_t workspace_bytes,
+              void* stream);
 
 /* Workspace bytes bs_dispatch needs for (T, k, E). */
 size_t bs_dispatch_workspace_bytes(int64_t T, int64_t k, int64_t E);

@@ -73,13 +73,29 @@ def router_logits_f64(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor)
     return x.double() @ weight.double().t() + bias.double()
 
 
-def near_tie_tokens(logits_f64: torch.Tensor, top_k: int, eps: float = 1e-6) -> torch.Tensor:
-    """Bool [T]: tokens whose k-th and (k+1)-th logits differ by <= eps, or whose
-    selected logits contain an internal tie (order ambiguity)."""
+def near_tie_tokens(logits_f64: torch.Tensor, top_k: int, eps: float = 1e-6,
+                    *approx_logits: torch.Tensor) -> torch.Tensor:
+    """Bool [T]: tokens whose top-k selection is not decidable.
+
+    A token is a near-tie when the gap between its k-th and (k+1)-th exact
+    (fp64) logits, or between two of its selected logits, is at most ``eps``
+    widened by the logit errors, on that token, of the fp32 implementations
+    being compared (``approx_logits``, each [T, E]): an ordering closer than
+    the sum of those errors can legitimately come out either way.
+    """
     srt = torch.sort(logits_f64, dim=-1, descending=True).values
     gap_k = srt[:, top_k - 1] - srt[:, top_k] if srt.shape[1] > top_k else torch.full_like(srt[:, 0], 1.0)
     inner = (srt[:, : top_k - 1] - srt[:, 1:top_k]).abs().min(dim=-1).values if top_k > 1 else torch.full_like(srt[:, 0], 1.0)
-    return (gap_k <= eps) | (inner <= eps)
+    band = torch.full_like(gap_k, eps)
+    for a in approx_logits:
+        band = band + (a.double() - logits_f64).abs().max(dim=-1).values
+    return (gap_k <= band) | (inner <= band)
+
+
+# Stated bound on the library router's logit error (both its tensor-core and
+# CUDA-core forms measure below 1.5e-5 at H = 2880); used to widen the tie band
+# where a test compares routings without the library's logits.
+ROUTER_LOGIT_ERR = 2e-5
 
 
 def _apply_gate_bf16(gate_up: torch.Tensor, limit: float, alpha: float) -> torch.Tensor:

@@ -60,10 +60,10 @@ def test_bad_shapes_are_rejected():
     st = lib.bs_moe_gate_up(p, p, 4, 4, 2, 48, 64, p, p, p, 0, 1.702, 7.0, p, 0, None)
     assert st == _lib.BS_ERR_INVALID_ARGUMENT and "multiple of 32" in _err(lib)
     # top_k larger than the expert count
-    st = lib.bs_router(p, 0, p, p, 1, 4, 64, 4, 8, None, p, p, 2, None)
+    st = lib.bs_router(p, 0, p, p, 1, 4, 64, 4, 8, None, p, p, 2, None, 0, None)
     assert st == _lib.BS_ERR_INVALID_ARGUMENT
     # unknown dtype code
-    st = lib.bs_router(p, 7, p, p, 1, 4, 64, 8, 2, None, p, p, 2, None)
+    st = lib.bs_router(p, 7, p, p, 1, 4, 64, 8, 2, None, p, p, 2, None, 0, None)
     assert st == _lib.BS_ERR_INVALID_ARGUMENT
 
 
