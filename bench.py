@@ -198,7 +198,7 @@ def run_reference(args, rank, world):
 # ---------------------------------------------------------------- our arm
 
 STAGES = ("router", "dispatch", "gate_up", "down", "combine")
-LAUNCHES = {"router": 3, "dispatch": 4, "gate_up": 1, "down": 1, "combine": 1}
+LAUNCHES = {"router": 3, "dispatch": 4, "gate_up": 1, "down": 1, "combine": 1}  # router: 2 at T <= 64
 
 
 def layer_stages(x, p, k, algo, bufs):

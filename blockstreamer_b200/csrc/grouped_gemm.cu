@@ -15,9 +15,15 @@
 //   * B (tokens): 128B-swizzled TMA tiles of 64 x 64 bf16 in shared memory.
 //   * D: fp32 accumulators in TMEM (up to 320 columns: one 128x256 and one
 //     128x64 MMA per K16 step), drained by four epilogue warps with tcgen05.ld.
-// Warp roles (448 threads): 0 TMA producer, 1 MMA issuer (+TMEM owner),
-// 2-5 epilogue, 6-13 dequant.  mbarrier pipelines link them; every wait is
-// bounded (timeout -> status word + clean exit, TMEM freed).
+// Warp roles (480 threads): 0 token-tile TMA producer, 1 MMA issuer (+TMEM
+// owner), 2-5 epilogue, 6-13 dequant, 14 weight TMA producer.  The MMA issuer
+// is the critical path (each tcgen05.mma costs ~100-150 cycles to issue into a
+// dependent accumulator, whatever its N), so its loop is kept minimal: two
+// barrier waits, four or eight MMAs with precomputed descriptors, one commit.  The token tiles
+// (4 x 40 KiB stages) and the weights (6 x 4 KiB e2m1 stages, 6 x 32 TMEM
+// columns) have separate rings so the dequant can run further ahead than the
+// large token stages allow.  Every wait is bounded (timeout -> status word +
+// clean exit, TMEM freed).
 // MODE 0: gate_up — bias + clamped interleaved SwiGLU (gptoss.py:130-135,158-166).
 // MODE 1: plain   — bias (gptoss.py:167-174) / mxfp4_matmul.
 #include <cudaTypedefs.h>
@@ -31,24 +37,25 @@ namespace {
 constexpr int kBM = 128;                       // weight rows per tile (MMA M)
 constexpr int kBK = 64;                        // K per pipeline stage
 constexpr int kNMax = 320;                     // token rows per tile
-constexpr int kStages = 4;
+constexpr int kStagesB = 4;                    // token-tile ring (shared memory)
+constexpr int kStagesA = 6;                    // weight ring (e2m1 bytes in smem, bf16 in TMEM)
 constexpr int kBoxRows = 64;                   // token rows per TMA box
 constexpr int kBoxBytes = kBoxRows * kBK * 2;  // 8 KiB
-constexpr int kBBytes = kNMax * kBK * 2;       // 40 KiB
-constexpr int kABytes = kBM * kBK / 2;         // 4 KiB of e2m1 bytes
-constexpr int kStageBytes = kBBytes + kABytes;
+constexpr int kBBytes = kNMax * kBK * 2;       // 40 KiB per token stage
+constexpr int kABytes = kBM * kBK / 2;         // 4 KiB of e2m1 bytes per weight stage
 constexpr int kMaxGroups = 128;                // K <= 4096
-constexpr int kScaleBufBytes = kBM * kMaxGroups;  // one tile's scale rows (16 KiB max)
-constexpr int kACol = 320;                     // TMEM column of the A ring
-constexpr int kTmemCols = 512;
+constexpr int kACol = 320;                   constexpr int kTmemCols = 512;
 constexpr int kDeqGroups = 2;
 constexpr int kWarpTMA = 0, kWarpMMA = 1, kWarpEpi0 = 2, kWarpDeq0 = 6;
-constexpr int kThreads = (kWarpDeq0 + 4 * kDeqGroups) * 32;
-// barriers: full, adone, empty per stage; sfull, sempty per scale buffer; accfull, accempty, drain
-constexpr int kNumBars = 3 * kStages + 4 + 3;
+constexpr int kWarpTMA_A = kWarpDeq0 + 4 * kDeqGroups;  // weight-ring producer
+constexpr int kThreads = (kWarpTMA_A + 1) * 32;
+// barriers: fullB per token stage; fullA, adone, emptyA per weight stage (emptyA
+// also frees the token stage of the same K step); sfull, sempty per scale
+// buffer; accfull, accempty, drain
+constexpr int kNumBars = kStagesB + 3 * kStagesA + 4 + 3;
 
-static_assert(kStageBytes % 1024 == 0, "stages must keep 1024-byte alignment for SW128");
-static_assert(kACol + kStages * (kBK / 2) <= kTmemCols, "TMEM budget");
+static_assert(kBBytes % 1024 == 0, "token stages must keep 1024-byte alignment for SW128");
+static_assert(kACol + kStagesA * (kBK / 2) <= kTmemCols, "TMEM budget");
 
 struct Tile {
   int e, mt, nrows, nmma;
@@ -124,6 +131,43 @@ __device__ __forceinline__ float swiglu_fast(float gate, float up, float alpha, 
   return (up + 1.0f) * __fdividef(gate, 1.0f + __expf(-alpha * gate));
 }
 
+// One 16-column chunk of the accumulator (one token per column) for the lane's
+// weight row: bias, then SwiGLU across the (gate, up) lane pair (MODE 0) or the
+// plain projection (MODE 1), stored as bf16.
+template <int MODE>
+__device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[16], int c0, const Tile& t, int row_w,
+                                               bool rv, float bv, float bp, int lane, int Nw,
+                                               float alpha, float limit, uint16_t* __restrict__ out) {
+  if (MODE == 0) {
+    // Lane pair (2i, 2i+1) holds the gate and up rows of one output column.
+    // The even lane produces the pair's even token columns, the odd lane the
+    // odd ones; each sends its partner the value the partner lacks.
+    const int odd = lane & 1;
+    const int Iout = Nw >> 1;
+    uint16_t* orow = out + (row_w >> 1);
+#pragma unroll
+    for (int jj = 0; jj < 8; ++jj) {
+      const uint32_t e0 = v[2 * jj], e1 = v[2 * jj + 1];
+      const uint32_t mine = odd ? e1 : e0;  // my row at my column
+      const uint32_t give = odd ? e0 : e1;  // my row at the partner's column
+      const uint32_t got = __shfl_xor_sync(0xffffffffu, give, 1);  // partner's row at my column
+      const float own = __uint_as_float(mine) + bv;
+      const float oth = __uint_as_float(got) + bp;
+      const float hv = odd ? swiglu_fast(oth, own, alpha, limit) : swiglu_fast(own, oth, alpha, limit);
+      const int n = c0 + 2 * jj + odd;
+      if (n < t.nrows && rv) orow[(t.r0 + n) * Iout] = __bfloat16_as_ushort(__float2bfloat16_rn(hv));
+    }
+  } else {
+    uint16_t* ocol = out + row_w;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int n = c0 + i;
+      if (n < t.nrows && rv)
+        ocol[(t.r0 + n) * Nw] = __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[i]) + bv));
+    }
+  }
+}
+
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1) tc_grouped_kernel(
     const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_a,
@@ -133,8 +177,10 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_kernel(
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint8_t* sbuf = smem + kStages * kStageBytes;  // [2][kScaleBufBytes]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sbuf + 2 * kScaleBufBytes);
+  uint8_t* asm_ring = smem + kStagesB * kBBytes;            // [kStagesA][kABytes]
+  uint8_t* sbuf = asm_ring + kStagesA * kABytes;            // [2][scale_buf]
+  const int scale_buf = (kBM * (K / 32) + 127) & ~127;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sbuf + 2 * scale_buf);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + kNumBars);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
   int* off = reinterpret_cast<int*>(tmem_holder + 2);
@@ -142,19 +188,21 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_kernel(
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
   auto bar = [&](int i) { return ptx::smem_addr(bars + i); };
-  auto full = [&](int s) { return bar(s); };
-  auto adone = [&](int s) { return bar(kStages + s); };
-  auto empty = [&](int s) { return bar(2 * kStages + s); };
-  auto sfull = [&](int b) { return bar(3 * kStages + b); };
-  auto sempty = [&](int b) { return bar(3 * kStages + 2 + b); };
-  const uint32_t accfull = bar(3 * kStages + 4), accempty = bar(3 * kStages + 5),
-                 drain = bar(3 * kStages + 6);
+  auto fullB = [&](int s) { return bar(s); };
+  auto fullA = [&](int s) { return bar(kStagesB + s); };
+  auto adone = [&](int s) { return bar(kStagesB + kStagesA + s); };
+  auto emptyA = [&](int s) { return bar(kStagesB + 2 * kStagesA + s); };
+  constexpr int kB0 = kStagesB + 3 * kStagesA;
+  auto sfull = [&](int b) { return bar(kB0 + b); };
+  auto sempty = [&](int b) { return bar(kB0 + 2 + b); };
+  const uint32_t accfull = bar(kB0 + 4), accempty = bar(kB0 + 5), drain = bar(kB0 + 6);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      ptx::mbar_init(full(s), 1);
+    for (int s = 0; s < kStagesB; ++s) ptx::mbar_init(fullB(s), 1);
+    for (int s = 0; s < kStagesA; ++s) {
+      ptx::mbar_init(fullA(s), 1);
       ptx::mbar_init(adone(s), 4);
-      ptx::mbar_init(empty(s), 1);
+      ptx::mbar_init(emptyA(s), 1);
     }
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(sfull(b), 1);
@@ -185,40 +233,67 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_kernel(
   const int total = ipre[E];
 
   if (warp == kWarpTMA) {
-    // ------------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------ token-tile producer
     if (lane == 0) {
-      int last_round[kStages];
-      for (int s = 0; s < kStages; ++s) last_round[s] = -1;
+      int last_round[kStagesB];
+      for (int s = 0; s < kStagesB; ++s) last_round[s] = -1;
+      uint32_t g = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; ok && item < total; item += gridDim.x) {
+        const Tile t = decode_item(off, ipre, E, MT, item);
+        const int nbox = (t.nmma + kBoxRows - 1) / kBoxRows;
+        for (int ks = 0; ks < KS; ++ks, ++g) {
+          const int s = g % kStagesB, r = g / kStagesB;
+          // stage s last held K step g - kStagesB; its MMAs are complete once the
+          // weight-ring barrier of that step has flipped (one commit per step)
+          if (g >= (uint32_t)kStagesB) {
+            const uint32_t gp = g - kStagesB;
+            if (!ptx::mbar_wait(emptyA(gp % kStagesA), (gp / kStagesA) & 1, abort_flag)) { ok = false; break; }
+          }
+          uint8_t* st = smem + s * kBBytes;
+          ptx::mbar_arrive_expect_tx(fullB(s), nbox * kBoxBytes);
+          for (int jb = 0; jb < nbox; ++jb)
+            ptx::tma_load_2d(ptx::smem_addr(st + jb * kBoxBytes), &tm_b, fullB(s), ks * kBK,
+                             (int)(t.r0 + jb * kBoxRows));
+          last_round[s] = r;
+        }
+      }
+      if (!ok) {  // let issued copies land before the CTA exits
+        for (int s = 0; s < kStagesB; ++s)
+          if (last_round[s] >= 0) ptx::mbar_wait(fullB(s), last_round[s] & 1, abort_flag, 200000000LL);
+      }
+    }
+    __syncwarp();
+  } else if (warp == kWarpTMA_A) {
+    // ------------------------------------------------------------ weight producer (e2m1 + scales)
+    if (lane == 0) {
+      int last_round[kStagesA];
+      for (int s = 0; s < kStagesA; ++s) last_round[s] = -1;
       int last_srnd[2] = {-1, -1};
       uint32_t g = 0, j = 0;
       bool ok = true;
       for (int item = blockIdx.x; ok && item < total; item += gridDim.x, ++j) {
         const Tile t = decode_item(off, ipre, E, MT, item);
-        const int nbox = (t.nmma + kBoxRows - 1) / kBoxRows;
         const int arow = t.e * Nw + t.mt * kBM;
         // the tile's scale rows: one contiguous run of valid_rows * G bytes
         const int b = j & 1, sr = j >> 1;
         if (!ptx::mbar_wait(sempty(b), (sr & 1) ^ 1, abort_flag)) { ok = false; break; }
         const int vrows = min(kBM, Nw - t.mt * kBM);
         ptx::mbar_arrive_expect_tx(sfull(b), (uint32_t)(vrows * G));
-        ptx::bulk_load(ptx::smem_addr(sbuf + b * kScaleBufBytes), scales + (int64_t)arow * G,
+        ptx::bulk_load(ptx::smem_addr(sbuf + b * scale_buf), scales + (int64_t)arow * G,
                        (uint32_t)(vrows * G), sfull(b));
         last_srnd[b] = sr;
         for (int ks = 0; ks < KS; ++ks, ++g) {
-          const int s = g % kStages, r = g / kStages;
-          if (!ptx::mbar_wait(empty(s), (r & 1) ^ 1, abort_flag)) { ok = false; break; }
-          uint8_t* st = smem + s * kStageBytes;
-          ptx::mbar_arrive_expect_tx(full(s), nbox * kBoxBytes + kABytes);
-          for (int jb = 0; jb < nbox; ++jb)
-            ptx::tma_load_2d(ptx::smem_addr(st + jb * kBoxBytes), &tm_b, full(s), ks * kBK,
-                             (int)(t.r0 + jb * kBoxRows));
-          ptx::tma_load_2d(ptx::smem_addr(st + kBBytes), &tm_a, full(s), ks * (kBK / 2), arow);
+          const int s = g % kStagesA, r = g / kStagesA;
+          if (!ptx::mbar_wait(emptyA(s), (r & 1) ^ 1, abort_flag)) { ok = false; break; }
+          ptx::mbar_arrive_expect_tx(fullA(s), kABytes);
+          ptx::tma_load_2d(ptx::smem_addr(asm_ring + s * kABytes), &tm_a, fullA(s), ks * (kBK / 2), arow);
           last_round[s] = r;
         }
       }
-      if (!ok) {  // let issued copies land before the CTA exits
-        for (int s = 0; s < kStages; ++s)
-          if (last_round[s] >= 0) ptx::mbar_wait(full(s), last_round[s] & 1, abort_flag, 200000000LL);
+      if (!ok) {
+        for (int s = 0; s < kStagesA; ++s)
+          if (last_round[s] >= 0) ptx::mbar_wait(fullA(s), last_round[s] & 1, abort_flag, 200000000LL);
         for (int b = 0; b < 2; ++b)
           if (last_srnd[b] >= 0) ptx::mbar_wait(sfull(b), last_srnd[b] & 1, abort_flag, 200000000LL);
       }
@@ -230,6 +305,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_kernel(
       uint32_t g = 0, j = 0;
       bool ok = true;
       bool issued = false;
+      const uint64_t bdesc0 = ptx::sdesc_kmajor_sw128(ptx::smem_addr(smem));
+      const uint32_t a_t0 = tbase + kACol;
       for (int item = blockIdx.x; ok && item < total; item += gridDim.x, ++j) {
         const Tile t = decode_item(off, ipre, E, MT, item);
         const uint32_t n1 = t.nmma < 256 ? t.nmma : 256, n2 = t.nmma - n1;
@@ -238,23 +315,37 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_kernel(
         if (!ptx::mbar_wait(accempty, (j & 1) ^ 1, abort_flag)) { ok = false; break; }
         ptx::tc_fence_after();
         for (int ks = 0; ks < KS; ++ks, ++g) {
-          const int s = g % kStages;
-          const uint32_t ph = (g / kStages) & 1;
-          if (!ptx::mbar_wait(full(s), ph, abort_flag) || !ptx::mbar_wait(adone(s), ph, abort_flag)) {
+          const int sb = g % kStagesB, sa = g % kStagesA;
+          // adone(sa) is signalled by the dequant warps only after they also saw
+          // this step's token tile land (fullB), so one wait covers both operands
+          if (!ptx::mbar_wait(adone(sa), (g / kStagesA) & 1, abort_flag)) {
             ok = false;
             break;
           }
           ptx::tc_fence_after();
-          const uint32_t bsm = ptx::smem_addr(smem + s * kStageBytes);
-#pragma unroll
-          for (int kk = 0; kk < kBK / 16; ++kk) {
-            const uint32_t acc = (ks > 0 || kk > 0) ? 1u : 0u;
-            const uint32_t a_t = tbase + kACol + s * (kBK / 2) + kk * 8;
-            ptx::mma_ts_bf16(tbase, a_t, ptx::sdesc_kmajor_sw128(bsm + kk * 32), id1, acc);
-            if (n2) ptx::mma_ts_bf16(tbase + 256, a_t, ptx::sdesc_kmajor_sw128(bsm + 256 * 128 + kk * 32),
-                                     id2, acc);
+          // descriptors advance by adding to the 16-byte start-address field
+          const uint64_t bd = bdesc0 + (uint64_t)((sb * kBBytes) >> 4);
+          const uint32_t at = a_t0 + sa * (kBK / 2);
+          const uint32_t acc0 = ks > 0 ? 1u : 0u;
+          if (n2) {
+            // two independent accumulators, issued alternately so that each
+            // MMA's dependency on its own accumulator overlaps the other's
+            const uint64_t bd2 = bd + (uint64_t)((256 * 128) >> 4);
+            ptx::mma_ts_bf16(tbase, at + 0, bd + 0, id1, acc0);
+            ptx::mma_ts_bf16(tbase + 256, at + 0, bd2 + 0, id2, acc0);
+            ptx::mma_ts_bf16(tbase, at + 8, bd + 2, id1, 1u);
+            ptx::mma_ts_bf16(tbase + 256, at + 8, bd2 + 2, id2, 1u);
+            ptx::mma_ts_bf16(tbase, at + 16, bd + 4, id1, 1u);
+            ptx::mma_ts_bf16(tbase + 256, at + 16, bd2 + 4, id2, 1u);
+            ptx::mma_ts_bf16(tbase, at + 24, bd + 6, id1, 1u);
+            ptx::mma_ts_bf16(tbase + 256, at + 24, bd2 + 6, id2, 1u);
+          } else {
+            ptx::mma_ts_bf16(tbase, at + 0, bd + 0, id1, acc0);
+            ptx::mma_ts_bf16(tbase, at + 8, bd + 2, id1, 1u);
+            ptx::mma_ts_bf16(tbase, at + 16, bd + 4, id1, 1u);
+            ptx::mma_ts_bf16(tbase, at + 24, bd + 6, id1, 1u);
           }
-          ptx::tc_commit(empty(s));
+          ptx::tc_commit(emptyA(sa));
           issued = true;
         }
         if (!ok) break;
@@ -269,7 +360,6 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_kernel(
   } else if (warp < kWarpDeq0) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
-    const int odd = lane & 1;
     uint32_t j = 0;
     for (int item = blockIdx.x; item < total; item += gridDim.x, ++j) {
       const Tile t = decode_item(off, ipre, E, MT, item);
@@ -280,38 +370,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_kernel(
       const float bv = rv ? bias_at(bias, bias_f32, (int64_t)t.e * Nw + row_w) : 0.f;
       const float bp = __shfl_xor_sync(0xffffffffu, bv, 1);
       const uint32_t taddr = tbase + ((uint32_t)(q * 32) << 16);
+      // One 16-column load per wait: issuing two loads before the wait made
+      // this loop ~3x slower on B200 (measured), so the loads stay single.
       for (int c0 = 0; c0 < t.nmma; c0 += 16) {
         uint32_t v[16];
         ptx::tmem_ld_32x32b_x16(taddr + c0, v);
         ptx::tmem_wait_ld();
-        if (MODE == 0) {
-          // Lane pair (2i, 2i+1) holds the gate and up rows of one output column.
-          // The even lane produces the pair's even token columns, the odd lane the
-          // odd ones; each sends its partner the value the partner lacks.
-          const int Iout = Nw >> 1;
-          uint16_t* orow = out + (row_w >> 1);
-#pragma unroll
-          for (int jj = 0; jj < 8; ++jj) {
-            const uint32_t e0 = v[2 * jj], e1 = v[2 * jj + 1];
-            const uint32_t mine = odd ? e1 : e0;     // my row at my column
-            const uint32_t give = odd ? e0 : e1;     // my row at the partner's column
-            const uint32_t got = __shfl_xor_sync(0xffffffffu, give, 1);  // partner's row at my column
-            const float own = __uint_as_float(mine) + bv;
-            const float oth = __uint_as_float(got) + bp;
-            const float hv = odd ? swiglu_fast(oth, own, alpha, limit) : swiglu_fast(own, oth, alpha, limit);
-            const int n = c0 + 2 * jj + odd;
-            if (n < t.nrows && rv)
-              orow[(t.r0 + n) * Iout] = __bfloat16_as_ushort(__float2bfloat16_rn(hv));
-          }
-        } else {
-          uint16_t* ocol = out + row_w;
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int n = c0 + i;
-            if (n < t.nrows && rv)
-              ocol[(t.r0 + n) * Nw] = __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[i]) + bv));
-          }
-        }
+        epilogue_chunk<MODE>(v, c0, t, row_w, rv, bv, bp, lane, Nw, alpha, limit, out);
       }
       ptx::tc_fence_before();
       __syncwarp();
@@ -329,16 +394,16 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_kernel(
       (void)decode_item(off, ipre, E, MT, item);
       const int b = j & 1;
       if (!warp_wait(sfull(b), (j >> 1) & 1, abort_flag)) { ok = false; break; }
-      const uint8_t* srow = sbuf + b * kScaleBufBytes + r * G;
+      const uint8_t* srow = sbuf + b * scale_buf + r * G;
       for (int ks = dg; ks < KS; ks += kDeqGroups) {
         const uint32_t g = gbase + ks;
-        const int s = g % kStages;
-        const uint32_t ph = (g / kStages) & 1;
+        const int s = g % kStagesA;
+        const uint32_t ph = (g / kStagesA) & 1;
         const int g0 = 2 * ks;
         const uint32_t s0 = srow[g0];
         const uint32_t s1 = (g0 + 1 < G) ? srow[g0 + 1] : 127u;
-        if (!warp_wait(full(s), ph, abort_flag)) { ok = false; break; }
-        const uint4* src = reinterpret_cast<const uint4*>(smem + s * kStageBytes + kBBytes + r * 32);
+        if (!warp_wait(fullA(s), ph, abort_flag)) { ok = false; break; }
+        const uint4* src = reinterpret_cast<const uint4*>(asm_ring + s * kABytes + r * 32);
         const uint4 b0 = src[0], b1 = src[1];
         const E2M1Pool p0 = make_e2m1_pool(s0), p1 = make_e2m1_pool(s1);
         uint32_t v[32];
@@ -353,7 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_kernel(
         ptx::tmem_st_32x32b_x32(taddr + s * (kBK / 2), v);
         ptx::tmem_wait_st();
         ptx::tc_fence_before();
-        __syncwarp();
+        if (!warp_wait(fullB(g % kStagesB), (g / kStagesB) & 1, abort_flag)) { ok = false; break; }
         if (lane == 0) ptx::mbar_arrive(adone(s));
       }
       __syncwarp();
@@ -397,8 +462,9 @@ int tc_grouped_launch(int mode, const void* x, const int32_t* offsets, int64_t r
                      (uint64_t)K * 2, kBK, kBoxRows, CU_TENSOR_MAP_SWIZZLE_128B));
   BS_TRY(make_map_2d(&tm_a, CU_TENSOR_MAP_DATA_TYPE_UINT8, blocks, (uint64_t)G * 16, (uint64_t)(E * N),
                      (uint64_t)G * 16, kBK / 2, kBM, CU_TENSOR_MAP_SWIZZLE_NONE));
-  const size_t smem = 1024 + (size_t)kStages * kStageBytes + 2 * kScaleBufBytes + kNumBars * 8 + 16 +
-                      (size_t)2 * (E + 1) * sizeof(int);
+  const size_t scale_buf = (size_t)((kBM * G + 127) & ~127);
+  const size_t smem = 1024 + (size_t)kStagesB * kBBytes + (size_t)kStagesA * kABytes + 2 * scale_buf +
+                      kNumBars * 8 + 16 + (size_t)2 * (E + 1) * sizeof(int);
   BS_REQUIRE(smem <= 227 * 1024, BS_ERR_CAPACITY, "tcgen05 GEMM: too many experts for shared memory");
   auto kern = mode == 0 ? tc_grouped_kernel<0> : tc_grouped_kernel<1>;
   BS_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
