@@ -253,7 +253,6 @@ def run_ours(args, rank, world, local):
     shape = CASES[key]
     dev = torch.device("cuda", torch.cuda.current_device())
     if world > 1:
-        from blockstreamer_b200.expert_parallel import run_bench_ep
         return run_bench_ep(args, rank, world, local, shape, case_id, T_total)
     T = T_total
     k = shape.top_k
@@ -385,6 +384,104 @@ def run_ours(args, rank, world, local):
         cb = cpu_sample(shape_c, p_c, x_c, experts_in_sample=1)
         line["cpu_baseline"] = {k2: cb[k2] for k2 in ("value", "unit", "cores", "kind", "sample")}
     if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- expert parallel (N > 1)
+
+def run_bench_ep(args, rank, world, local, shape, case_id, T_total):
+    """The same layer split over `world` ranks: experts [r*E/R, (r+1)*E/R) and
+    T/R tokens per rank (strong scaling: the 8192-token batch is fixed)."""
+    import torch.distributed as dist
+    from blockstreamer_b200.expert_parallel import ExpertParallelMoE, shard_experts
+
+    dev = torch.device("cuda", local)
+    if T_total % world:
+        raise SystemExit(f"{T_total} tokens do not split over {world} ranks")
+    Tr = T_total // world
+    full = make_layer(shape, case_id, device=dev)
+    router_w, router_b = full["router.weight"], full["router.bias"]
+    local_p = shard_experts({k.split(".", 1)[1]: v for k, v in full.items() if k.startswith("experts.")},
+                            rank, world)
+    del full
+    x_all = make_tokens(T_total, shape.hidden, case_id, device=dev)
+    x = x_all[rank * Tr:(rank + 1) * Tr].contiguous()
+    del x_all
+    torch.cuda.empty_cache()
+    layer = ExpertParallelMoE(shape.experts, shape.top_k)
+
+    def step():
+        return layer(x, router_w, router_b, local_p)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier(world)
+        torch.cuda.synchronize()
+        ev0.record(st)
+        for _ in range(args.steps):
+            step()
+        ev1.record(st)
+        torch.cuda.synchronize()
+        barrier(world)
+    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world)
+    value = T_total / (ms * 1e-3)
+    # per-stage breakdown (same steps, events at stage boundaries)
+    stage_ms = {}
+    for _ in range(args.steps):
+        layer.marks = []
+        step()
+        torch.cuda.synchronize()
+        for (_, a), (name, b) in zip(layer.marks[:-1], layer.marks[1:]):
+            stage_ms[name] = stage_ms.get(name, 0.0) + a.elapsed_time(b) / args.steps
+    layer.marks = None
+    # e2e: this rank's tokens in from pinned host memory, its output back out
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty_like(x_host).pin_memory()
+    x_dev = torch.empty_like(x)
+    e2e = []
+    for i in range(args.warmup + args.steps):
+        barrier(world)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        x_dev.copy_(x_host, non_blocking=True)
+        o, _, _ = layer(x_dev, router_w, router_b, local_p)
+        out_host.copy_(o, non_blocking=True)
+        b.record(st)
+        b.synchronize()
+        if i >= args.warmup:
+            e2e.append(a.elapsed_time(b))
+    e2e_ms = max_over_ranks(statistics.mean(e2e), world)
+    stats = layer.last_stats
+    peaks, peak_src = load_peaks()
+    S_local = sum(stats.rows_received)
+    exp_ms = stage_ms.get("experts", 0.0)
+    exp_flops = S_local * 6.0 * shape.hidden * shape.intermediate
+    achieved = exp_flops / (exp_ms * 1e-3) / 1e12 if exp_ms else 0.0
+    peak = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": args.workload, "tokens": T_total, "tokens_per_rank": Tr,
+                           "experts_per_rank": shape.experts // world, "parallelism": f"ep{world}",
+                           "collective": "NCCL all_to_all_single (counts, dispatch rows, combine rows)",
+                           "l2": "inputs larger than L2 (expert weights + dispatched rows per rank)",
+                           "rank0_rows_sent": stats.rows_sent,
+                           "rank0_rows_received": stats.rows_received},
+                "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                             "frac": achieved / peak if peak else None, "traffic": None,
+                             "kernel": "experts (gate_up + down, rank 0)",
+                             "peak_source": f"{peak_src} bf16 dense sustained (cuBLAS)"},
+                "layer_roofline": {"stage_ms_rank0": stage_ms},
+                "e2e": {"value": T_total / (e2e_ms * 1e-3), "unit": "tokens/s",
+                        "h2d_bytes_per_step": x.numel() * 2 * world,
+                        "d2h_bytes_per_step": x.numel() * 2 * world,
+                        "api": "blockstreamer_b200.expert_parallel.ExpertParallelMoE"},
+                "clocks": clk.summary(), "gpu_launches": 14 * args.steps}
         print(json.dumps(line), flush=True)
 
 

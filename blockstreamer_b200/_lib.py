@@ -43,6 +43,8 @@ SIGNATURES = {
     "bs_moe_gate_up": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _i32, _f32,
                               _f32, _vp, _i32, _vp]),
     "bs_moe_down": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _i32, _vp, _i32, _vp]),
+    "bs_ep_regroup": (_i32, [_vp, _i64, _i64, _vp, _i64, _i64, _vp, _vp, _vp, _vp]),
+    "bs_gather_rows": (_i32, [_vp, _vp, _i64, _i64, _vp, _vp]),
     "bs_combine": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp]),
     "bs_mxfp4_matmul": (_i32, [_vp, _i64, _i64, _vp, _vp, _i64, _vp, _vp, _i32, _vp]),
     "bs_moe_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64]),

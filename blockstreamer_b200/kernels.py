@@ -215,6 +215,36 @@ def combine(y: torch.Tensor, row_of_slot: torch.Tensor, weights: torch.Tensor, n
     return out
 
 
+def ep_regroup(recv_counts: torch.Tensor, x_recv: torch.Tensor, out: torch.Tensor | None = None):
+    """Expert-major regroup of all-to-all-received rows (see bs_ep_regroup).
+
+    recv_counts [R, El] int32 on the device; returns (x_grouped, expert_offsets [El+1], row_map)."""
+    _cuda("ep_regroup", recv_counts, x_recv)
+    R, El = recv_counts.shape
+    rows, H = x_recv.shape
+    dev = x_recv.device
+    x_grouped = out if out is not None else torch.empty_like(x_recv)
+    offsets = torch.empty(El + 1, dtype=torch.int32, device=dev)
+    row_map = torch.empty(max(rows, 1), dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        _lib.call("bs_ep_regroup", _p(_contig("recv_counts", recv_counts.to(torch.int32))), R, El,
+                  _p(_contig("x_recv", x_recv)), rows, H, _p(x_grouped), _p(offsets), _p(row_map),
+                  _stream(x_recv))
+    return x_grouped, offsets, row_map[:rows]
+
+
+def gather_rows(src: torch.Tensor, row_map: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """dst[i] = src[row_map[i]] (rows of bf16)."""
+    _cuda("gather_rows", src, row_map)
+    rows = row_map.numel()
+    H = src.shape[1]
+    dst = out if out is not None else torch.empty(rows, H, dtype=src.dtype, device=src.device)
+    with torch.cuda.device(src.device):
+        _lib.call("bs_gather_rows", _p(_contig("src", src)), _p(_contig("row_map", row_map)), rows, H,
+                  _p(dst), _stream(src))
+    return dst
+
+
 def mxfp4_matmul(x: torch.Tensor, blocks: torch.Tensor, scales: torch.Tensor,
                  bias: torch.Tensor | None = None, algo=ALGO_AUTO) -> torch.Tensor:
     """x [m, K] bf16 @ dequant(W) for one expert W = blocks [N, K/32, 16] -> [m, N] bf16."""

@@ -148,6 +148,22 @@ int bs_moe_down(const void* h, const int32_t* expert_offsets, int64_t rows_total
 int bs_combine(const void* y, const int32_t* row_of_slot, const float* weights, int64_t T,
                int64_t k, int64_t H, void* out, void* stream);
 
+/* Expert parallelism: regroup the rows an all-to-all delivered.
+ * No single-GPU counterpart in the reference (it has no expert parallelism);
+ * it serves the multi-GPU form of block_streamer/gptoss.py:149-176.
+ * recv_counts [R, El] int32 (device): rows from source rank s for local expert e,
+ * laid out source-major in x_recv [rows, H] bf16.  Writes x_grouped [rows, H]
+ * in expert-major order (within an expert: by source rank, then arrival order),
+ * expert_offsets [El+1] and row_map [rows] (received row -> grouped row).
+ * x_recv/x_grouped may both be NULL to compute only the maps. */
+int bs_ep_regroup(const int32_t* recv_counts, int64_t R, int64_t El, const void* x_recv,
+                  int64_t rows, int64_t H, void* x_grouped, int32_t* expert_offsets,
+                  int32_t* row_map, void* stream);
+
+/* dst[i] = src[row_map[i]] for i < rows, rows of H bf16 (undoes bs_ep_regroup). */
+int bs_gather_rows(const void* src, const int32_t* row_map, int64_t rows, int64_t H, void* dst,
+                   void* stream);
+
 /* One expert projection without activation: out[m, N] = x[m, K] @ dequant(W) (+ bias).
  * Replaces block_streamer/gptoss.py:74-75 (mxfp4_matmul forward) for one expert:
  * blocks [N, K/32, 16], scales [N, K/32], x [m, K] bf16, out [m, N] bf16;
