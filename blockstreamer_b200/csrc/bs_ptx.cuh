@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cuda.h>
+#include <cuda_fp16.h>
 #include <stdint.h>
 
 namespace bs {
@@ -65,6 +66,15 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, uint
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, uint32_t bar, int x,
+                                            int y, int z) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(bar)
       : "memory");
 }
 
@@ -176,8 +186,149 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t v[32
 __device__ __forceinline__ void tmem_wait_ld() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
+__device__ __forceinline__ void tmem_st_32x32b_x4(uint32_t taddr, uint32_t a, uint32_t b, uint32_t c,
+                                                  uint32_t d) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(taddr), "r"(a),
+               "r"(b), "r"(c), "r"(d)
+               : "memory");
+}
+
+// ---------------------------------------------------------------- block-scaled MMA
+// D[tmem] (+)= (A * SFA) * (B * SFB)^T with kind::mxf8f6f4: A e2m1 (the
+// checkpoint's codes, in the 16-byte-padded shared-memory form: 16 codes in
+// the low 8 bytes of every 16-byte chunk), B e4m3, one e8m0 scale per 32 K
+// elements of every row, M=128, K=32 per instruction.  The scale factors sit
+// in TMEM: for M=128, row r of A at lane (r % 32) of every 32-lane
+// subpartition, column (r / 32), byte `sf_id`; B the same with its N rows.
+__host__ __device__ __forceinline__ uint32_t idesc_mx_e2m1_e4m3(uint32_t N, uint32_t sfa_id,
+                                                               uint32_t sfb_id) {
+  return (sfb_id << 4) | (5u << 7) /* A e2m1 */ | (0u << 10) /* B e4m3 */ | ((N >> 3) << 17) |
+         (1u << 23) /* e8m0 scales */ | ((128u >> 4) << 24) | (sfa_id << 29);
+}
+__device__ __forceinline__ void mma_mx_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+
+// D[tmem] (+)= (A * SFA) * (B * SFB)^T with kind::mxf4: A and B both e2m1,
+// packed two codes per byte (low nibble first, as the checkpoint stores them),
+// K-major, K = 64 per instruction, one e8m0 scale per 32 K elements (two per
+// row per instruction, in bytes sf_id and sf_id + 1 of the TMEM word; sf_id
+// is 0 or 2).  TMEM layout of the scale factors as for mxf8f6f4 above.
+__host__ __device__ __forceinline__ uint32_t idesc_mxf4(uint32_t N, uint32_t sfa_id, uint32_t sfb_id) {
+  return (sfb_id << 4) | (1u << 7) /* A e2m1 */ | (1u << 10) /* B e2m1 */ | ((N >> 3) << 17) |
+         (1u << 23) /* e8m0 scales */ | ((128u >> 4) << 24) | (sfa_id << 29);
+}
+__device__ __forceinline__ void mma_mxf4_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_32x32b_x8(uint32_t taddr, const uint32_t v[8]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"r"(taddr),
+               "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t v[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+      "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+
+// Shared memory -> TMEM copy of a 32-row x 16-byte block (row l at byte
+// l * 16), written to lanes l, 32 + l, 64 + l, 96 + l (all four 32-lane
+// subpartitions) and columns c..c+3; executes in order with the issuing
+// thread's tcgen05.mma.
+__device__ __forceinline__ void tc_cp_32x128b_warpx4(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+// Descriptor of an unswizzled K-major block of 16-byte rows, 8-row core
+// matrices 128 bytes apart.
+__device__ __forceinline__ uint64_t sdesc_rows16(uint32_t saddr) {
+  return (uint64_t)((saddr & 0x3FFFFu) >> 4) | (1ull << 16) | ((uint64_t)(128 >> 4) << 32) | (1ull << 46);
+}
+
+// ---------------------------------------------------------------- e2m1
+// Two floats -> one byte of two e2m1 codes (round to nearest even, saturating
+// at +-6): `lo` in the low nibble.
+__device__ __forceinline__ uint32_t e2m1x2_from_f32(float lo, float hi) {
+  uint32_t r;
+  asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\tmov.b32 %0, {t, t, t, t};\n\t}"
+      : "=r"(r)
+      : "f"(hi), "f"(lo));
+  return r & 0xFFu;
+}
+// The low-nibble code of a byte -> float (exact).
+__device__ __forceinline__ float e2m1_lo_to_f32(uint32_t byte) {
+  uint32_t h2;
+  asm("{\n\t.reg .b8 t0, t1, t2, t3;\n\tmov.b32 {t0, t1, t2, t3}, %1;\n\tcvt.rn.f16x2.e2m1x2 %0, t0;\n\t}"
+      : "=r"(h2)
+      : "r"(byte));
+  return __half2float(__ushort_as_half((unsigned short)(h2 & 0xFFFFu)));
+}
+
+// ---------------------------------------------------------------- cp.async (LDGSTS)
+__device__ __forceinline__ void cp_async_8(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// The mbarrier receives one arrival once all of this thread's prior cp.async
+// copies have landed (its expected count must include that arrival).
+__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// Generic-proxy writes to shared memory (st.shared, completed cp.async) made
+// visible to the async proxy (tensor-core operand reads).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ---------------------------------------------------------------- e4m3
+// Two floats -> two e4m3 bytes (round to nearest even, saturating): `lo` in
+// the low byte.
+__device__ __forceinline__ uint32_t e4m3x2_from_f32(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// Two e4m3 bytes (low byte first) -> two floats (exact).
+__device__ __forceinline__ void e4m3x2_to_f32(uint32_t v, float& lo, float& hi) {
+  uint32_t h2;
+  asm("{\n\t.reg .b16 t;\n\tcvt.u16.u32 t, %1;\n\tcvt.rn.f16x2.e4m3x2 %0, t;\n\t}" : "=r"(h2) : "r"(v));
+  lo = __half2float(__ushort_as_half((unsigned short)(h2 & 0xFFFFu)));
+  hi = __half2float(__ushort_as_half((unsigned short)(h2 >> 16)));
+}
 
 }  // namespace ptx
+
+// Host: encode a 3-D tiled TMA descriptor (runtime.cu): dims innermost first,
+// strides in bytes of dims 1 and 2.
+int make_map_3d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, const uint64_t dims[3],
+                const uint64_t strides[2], const uint32_t box[3], CUtensorMapSwizzle sw);
 
 // Host: encode a 2-D tiled TMA descriptor (runtime.cu).  `inner` is the
 // contiguous extent in elements, `row_bytes` the pitch of the outer dimension.

@@ -28,6 +28,14 @@ int tc_grouped_launch(int mode, const void* x, const int32_t* offsets, int64_t r
                       const void* blocks, const void* scales, const void* bias, int bias_f32,
                       float alpha, float limit, void* out, cudaStream_t st);
 bool tc_supported(const void* scales, int64_t K, int64_t N);
+// Decode path (decode.cu): router + dispatch + block-scaled expert MMAs + combine, T <= 64.
+bool decode_supported(int64_t T, int64_t H, int64_t I, int64_t E, int64_t k);
+size_t decode_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t k);
+int decode_forward(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, int64_t k,
+                   const void* rw, const void* rb, int rdt, float* scores, int32_t* indices,
+                   const void* gu_b, const void* gu_s, const void* gu_bias, const void* dn_b,
+                   const void* dn_s, const void* dn_bias, int bias_f32, float alpha, float limit,
+                   void* out, void* ws, cudaStream_t st);
 
 namespace {
 
@@ -165,8 +173,18 @@ extern "C" int bs_mxfp4_matmul(const void* x, int64_t m, int64_t K, const void* 
   return tc_grouped_launch(1, x, nullptr, m, m, 1, K, N, blocks, scales, bias, 0, 0.f, 0.f, out, st);
 }
 
+namespace bs {
+namespace {
+size_t moe_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t k) {
+  size_t n = carve(nullptr, T, H, I, E, k).total;
+  if (decode_supported(T, H, I, E, k)) n = std::max(n, decode_workspace_bytes(T, H, I, E, k));
+  return n;
+}
+}  // namespace
+}  // namespace bs
+
 extern "C" size_t bs_moe_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t k) {
-  return bs::carve(nullptr, T, H, I, E, k).total;
+  return bs::moe_workspace_bytes(T, H, I, E, k);
 }
 
 extern "C" int bs_moe_forward(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, int64_t k,
@@ -182,14 +200,35 @@ extern "C" int bs_moe_forward(const void* x, int64_t T, int64_t H, int64_t I, in
   BS_ARG(T >= 0 && H > 0 && I > 0 && E > 0 && k > 0 && k <= E, "bs_moe_forward: bad sizes");
   BS_ARG((router_weight == nullptr) == (router_bias == nullptr),
          "bs_moe_forward: router weight and bias go together");
+  BS_ARG(algo >= BS_ALGO_AUTO && algo <= BS_ALGO_MX, "bs_moe_forward: unknown algo %d", algo);
   if (T == 0) return BS_OK;
-  const Workspace w = carve(workspace, T, H, I, E, k);
   BS_ARG(workspace, "bs_moe_forward: null workspace");
+  BS_ALIGNED16(workspace, "workspace");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // AUTO takes the decode path whenever it applies (T <= 64, aligned blocks).
+  const bool mx = algo == BS_ALGO_MX ||
+                  (algo == BS_ALGO_AUTO && decode_supported(T, H, I, E, k) &&
+                   ((uintptr_t)gate_up_blocks | (uintptr_t)down_blocks | (uintptr_t)gate_up_scales |
+                    (uintptr_t)down_scales) % 16 == 0);
+  if (mx) {
+    BS_ARG(decode_supported(T, H, I, E, k),
+           "bs_moe_forward: BS_ALGO_MX needs T <= 64, H and I multiples of 64, E <= 1024, k <= 32");
+    BS_ARG(router_dtype == BS_F32 || router_dtype == BS_BF16 || !router_weight,
+           "bs_moe_forward: router dtype must be bf16 or f32");
+    BS_ARG(bias_dtype == BS_BF16 || bias_dtype == BS_F32, "bs_moe_forward: bias dtype must be bf16 or f32");
+    const size_t need = decode_workspace_bytes(T, H, I, E, k);
+    BS_REQUIRE(workspace_bytes >= need, BS_ERR_CAPACITY,
+               "bs_moe_forward: workspace of %zu bytes is smaller than the %zu needed", workspace_bytes,
+               need);
+    BS_TRY(check_device());
+    return decode_forward(x, T, H, I, E, k, router_weight, router_bias, router_dtype, scores, indices,
+                          gate_up_blocks, gate_up_scales, gate_up_bias, down_blocks, down_scales,
+                          down_bias, bias_dtype == BS_F32, alpha, limit, out, workspace, st);
+  }
+  const Workspace w = carve(workspace, T, H, I, E, k);
   BS_REQUIRE(workspace_bytes >= w.total, BS_ERR_CAPACITY,
              "bs_moe_forward: workspace of %zu bytes is smaller than the %zu needed",
              workspace_bytes, w.total);
-  BS_ALIGNED16(workspace, "workspace");
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   if (router_weight)
     BS_TRY(router_launch(x, BS_BF16, router_weight, router_bias, router_dtype, T, H, E, k, nullptr,
                          scores, indices, BS_I32, w.router, w.router_bytes, st));

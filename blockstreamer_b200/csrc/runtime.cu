@@ -117,6 +117,20 @@ int make_map_2d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64
   return BS_OK;
 }
 
+int make_map_3d(CUtensorMap* m, CUtensorMapDataType dt, const void* base, const uint64_t dims[3],
+                const uint64_t strides[2], const uint32_t box[3], CUtensorMapSwizzle sw) {
+  auto fn = encode_fn();
+  BS_REQUIRE(fn, BS_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+  cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
+  cuuint64_t st[2] = {strides[0], strides[1]};
+  cuuint32_t bx[3] = {box[0], box[1], box[2]};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(m, dt, 3, const_cast<void*>(base), d, st, bx, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  BS_REQUIRE(r == CUDA_SUCCESS, BS_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed (%d)", (int)r);
+  return BS_OK;
+}
+
 }  // namespace bs
 
 extern "C" int bs_version(void) { return 1; }

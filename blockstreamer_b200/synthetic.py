@@ -73,8 +73,8 @@ def make_layer(shape: LayerShape, case_id: int, device="cpu") -> dict[str, torch
         "experts.gate_up_proj_blocks": u8(3, (E, 2 * I, G, 16), 0, 255),
         "experts.gate_up_proj_scales": u8(4, (E, 2 * I, G), shape.scale_lo, shape.scale_hi),
         "experts.gate_up_proj_bias": normal(5, (E, 2 * I), 0.02, torch.bfloat16),
-        "experts.down_proj_blocks": u8(6, (E, H, G, 16), 0, 255),
-        "experts.down_proj_scales": u8(7, (E, H, G), shape.scale_lo, shape.scale_hi),
+        "experts.down_proj_blocks": u8(6, (E, H, I // 32, 16), 0, 255),
+        "experts.down_proj_scales": u8(7, (E, H, I // 32), shape.scale_lo, shape.scale_hi),
         "experts.down_proj_bias": normal(8, (E, H), 0.02, torch.bfloat16),
     }
 
@@ -107,7 +107,8 @@ def expert_bytes(shape: LayerShape) -> int:
     """Packed bytes of one expert (blocks + scales + bias, both projections)."""
     H, I, G = shape.hidden, shape.intermediate, shape.groups
     gu = 2 * I * G * 16 + 2 * I * G + 2 * I * 2
-    dn = H * G * 16 + H * G + H * 2
+    Gd = I // 32
+    dn = H * Gd * 16 + H * Gd + H * 2
     return gu + dn
 
 

@@ -48,7 +48,9 @@ enum bs_dtype { BS_BF16 = 0, BS_F32 = 1, BS_I32 = 2, BS_I64 = 3 };
 enum bs_algo {
   BS_ALGO_AUTO = 0,     /* pick by tokens per expert                                  */
   BS_ALGO_GEMV = 1,     /* CUDA-core dequant-GEMV (decode shapes, HBM-bound)          */
-  BS_ALGO_TCGEN05 = 2   /* tcgen05/TMEM grouped GEMM (prefill shapes)                 */
+  BS_ALGO_TCGEN05 = 2,  /* tcgen05/TMEM grouped GEMM (prefill shapes)                 */
+  BS_ALGO_MX = 3        /* bs_moe_forward only, T <= 64: tcgen05 block-scaled MMAs on  */
+                        /* the e2m1 codes (activations as four e2m1 terms)            */
 };
 
 /* Library identity. */
@@ -177,7 +179,11 @@ int bs_mxfp4_matmul(const void* x, int64_t m, int64_t K, const void* blocks, con
  *  - router_weight/router_bias non-NULL: computes scores/indices into the
  *    caller's `scores` [T,k] f32 and `indices` [T,k] int32 buffers.
  *  - router_weight NULL: `scores` and `indices` are inputs.
- * Workspace: bs_moe_workspace_bytes(T, H, I, E, k). */
+ *  - algo BS_ALGO_MX (T <= 64; also what BS_ALGO_AUTO picks there): the
+ *    decode path -- four launches chained with programmatic dependent launch;
+ *    the expert projections run on tcgen05 block-scaled MMAs that read the
+ *    e2m1 codes and e8m0 scales as stored.
+ * Workspace: bs_moe_workspace_bytes(T, H, I, E, k) (covers every algo). */
 size_t bs_moe_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t k);
 int bs_moe_forward(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, int64_t k,
                    const void* router_weight, const void* router_bias, int router_dtype,
