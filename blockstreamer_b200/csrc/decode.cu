@@ -28,15 +28,18 @@
 //  4. decode_combine_kernel out[t] = bf16(sum over the k slots), fp32 sum.
 //
 // Work item of 2/3: 128 weight rows of one expert and a group of up to 16 of
-// its tokens (an expert with more tokens has several groups; the route
-// kernel lists them).
-// One CTA per SM: warp 4 issues the TMA copies (weight tiles [128 rows x 256
-// codes] as stored, the B term rows, per-item scale blocks); warps 0-3 repack
-// each item's scales into the 32-row blocks tcgen05.cp reads and drain the
-// accumulators; warp 5 copies every stage's scale factors into TMEM
-// (tcgen05.cp, ordered with its MMAs) and issues the MMAs.
+// its tokens (the route kernel lists the groups).  One CTA per SM: warp 4
+// issues the TMA copies (weight tiles [128 rows x 256 codes] as stored, the B
+// term rows, per-item scale blocks), warp 5 the MMAs, warps 6-9 (one per
+// 32-lane TMEM subpartition) write every stage's scale factors into TMEM with
+// tcgen05.st, warps 0-3 drain the accumulators.  On this GPU each
+// tcgen05.mma, tcgen05.cp and tcgen05.commit takes ~100 cycles of the tensor
+// pipe, so the scale factors stay out of it: the pipe runs 4 MMAs + 1 commit
+// per 16 KB stage, less than the stage's HBM time.
 #include "bs_common.cuh"
 #include "bs_ptx.cuh"
+
+#include <initializer_list>
 
 namespace bs {
 namespace {
@@ -46,12 +49,14 @@ constexpr int kTerms = 4;       // e2m1 terms per activation
 constexpr int kRTok = 16;       // tokens per router CTA
 constexpr int kKC = 256;        // K elements per pipeline stage: 128 bytes of codes per row, 4 MMAs
 constexpr int kBM = 128;        // weight rows per item (MMA M)
-constexpr int kThreads = 192;   // warps 0-3 scale repack + epilogue, 4 TMA, 5 MMA
+constexpr int kThreads = 320;   // warps 0-3 epilogue, 4 TMA, 5 MMA, 6-9 scale factors
 constexpr int kTmemCols = 512;
-constexpr int kSfStageCols = 16;  // per stage: SFA and SFB, 2 groups of four k-blocks x 4 columns
+constexpr int kSfStageCols = 24;  // per stage: SFA 2 groups x 4 columns, SFB 2 groups x 4 or 8 columns
 constexpr int kMaxStages = 12;
-constexpr int kGroupTok = 16;     // tokens per group: B = 4 terms x 16 = 64 rows at most
+constexpr int kMaxRing = 4;       // per-item buffers
+constexpr int kGroupTok = 16;     // tokens per group: an item's B is 4 x 16 = 64 rows at most
 constexpr int kMaxGroups = 1024 + 2048 / kGroupTok;
+constexpr int kRankMax = 8192;    // token x expert logits ranked in shared memory (32 KB)
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
@@ -99,14 +104,14 @@ template <> __device__ __forceinline__ float ldf<__nv_bfloat16>(const __nv_bfloa
   return __bfloat162float(*p);
 }
 
-// One warp: top-k of E values (ties -> lower index), softmax over the k.
-template <typename Get>
-__device__ void warp_topk(Get get, int E, int k, float* scores, int32_t* idx) {
+// One warp: top-k of E <= 32 PER values (ties -> lower index), softmax over
+// the k (modeling_gpt_oss.py:126-130).  Lane l holds experts l + 32 i.
+template <int PER, typename Get>
+__device__ void warp_topk(Get get, int E, int k, float* scores, int* idx) {
   const int lane = threadIdx.x & 31;
-  constexpr int kPer = 1024 / 32;
-  float v[kPer];
+  float v[PER];
 #pragma unroll
-  for (int i = 0; i < kPer; ++i) {
+  for (int i = 0; i < PER; ++i) {
     const int e = lane + 32 * i;
     v[i] = (e < E) ? get(e) : -INFINITY;
     if (v[i] != v[i]) v[i] = -INFINITY;
@@ -114,27 +119,29 @@ __device__ void warp_topk(Get get, int E, int k, float* scores, int32_t* idx) {
   float sel_v = 0.f;
   int sel_e = 0;
   for (int j = 0; j < k; ++j) {
-    float bv = -INFINITY;
+    float bv = __int_as_float(0x7fc00000u);  // NaN: below everything, never wins
     int be = 0x7fffffff;
 #pragma unroll
-    for (int i = 0; i < kPer; ++i) {
+    for (int i = 0; i < PER; ++i) {
       const int e = lane + 32 * i;
-      if (e < E && (v[i] > bv || (v[i] == bv && e < be))) {
-        bv = v[i];
-        be = e;
+      if (e < E && (v[i] > bv || bv != bv || (v[i] == bv && e < be))) {
+        if (v[i] == v[i]) {
+          bv = v[i];
+          be = e;
+        }
       }
     }
 #pragma unroll
     for (int off = 16; off; off >>= 1) {
       const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
       const int oe = __shfl_xor_sync(0xffffffffu, be, off);
-      if (ov > bv || (ov == bv && oe < be)) {
+      if (ov == ov && (bv != bv || ov > bv || (ov == bv && oe < be))) {
         bv = ov;
         be = oe;
       }
     }
 #pragma unroll
-    for (int i = 0; i < kPer; ++i)
+    for (int i = 0; i < PER; ++i)
       if (lane + 32 * i == be) v[i] = __int_as_float(0x7fc00000u);  // removed: never selected again
     if (lane == j) {
       sel_v = bv;
@@ -147,25 +154,42 @@ __device__ void warp_topk(Get get, int E, int k, float* scores, int32_t* idx) {
 #pragma unroll
   for (int off = 16; off; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
   if (lane < k) {
-    scores[lane] = ex / sum;
+    if (scores) scores[lane] = ex / sum;
     idx[lane] = sel_e;
   }
 }
 
+template <typename Get>
+__device__ void warp_topk_any(Get get, int E, int k, float* scores, int* idx) {
+  if (E <= 32) warp_topk<1>(get, E, k, scores, idx);
+  else if (E <= 64) warp_topk<2>(get, E, k, scores, idx);
+  else if (E <= 128) warp_topk<4>(get, E, k, scores, idx);
+  else if (E <= 256) warp_topk<8>(get, E, k, scores, idx);
+  else if (E <= 512) warp_topk<16>(get, E, k, scores, idx);
+  else warp_topk<32>(get, E, k, scores, idx);
+}
+
+__device__ __forceinline__ void load4(const float* p, float (&w)[4]) {
+  const float4 q = *reinterpret_cast<const float4*>(p);
+  w[0] = q.x, w[1] = q.y, w[2] = q.z, w[3] = q.w;
+}
+__device__ __forceinline__ void load4(const __nv_bfloat16* p, float (&w)[4]) {
+  const uint2 q = *reinterpret_cast<const uint2*>(p);
+  w[0] = bf16lo(q.x), w[1] = bf16hi(q.x), w[2] = bf16lo(q.y), w[3] = bf16hi(q.y);
+}
+
 // ------------------------------------------------------------------ 1. route
+// x -> four e2m1 terms and, with router weights, the router logits
+// (modeling_gpt_oss.py:126: linear + bias in the weights' dtype); top-k and
+// the dispatch run in the prologue of every gate_up CTA (route_dispatch).
 // xq: rows (4 t + term) of H/2 bytes (two codes per byte, low nibble first);
 // xs: rows (4 t + term) of gp bytes (one e8m0 scale per 32 values).
 template <typename WT>
 __global__ void __launch_bounds__(256) decode_route_kernel(
     const __nv_bfloat16* __restrict__ x, const WT* __restrict__ W, const WT* __restrict__ b,
-    int T, int H, int E, int k, int bf16_logits, float* __restrict__ logits,
-    float* __restrict__ scores, int32_t* __restrict__ idx, int* __restrict__ offsets,
-    int* __restrict__ row_of_slot, int* __restrict__ slot_of_row, int2* __restrict__ groups,
-    uint8_t* __restrict__ xq, uint8_t* __restrict__ xs, int gp, DecodeMeta* meta, int* status) {
+    int T, int H, int E, int bf16_logits, float* __restrict__ logits, uint8_t* __restrict__ xq,
+    uint8_t* __restrict__ xs, int gp) {
   __shared__ float red[8][kRTok];
-  __shared__ int cnt[1024];
-  __shared__ int off[1025];
-  __shared__ int is_last;
   pdl_wait();  // x comes from the previous kernel in the stream
   pdl_launch();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -198,7 +222,7 @@ __global__ void __launch_bounds__(256) decode_route_kernel(
       }
   }
 
-  if (W) {  // logits of expert blockIdx.x for 16 tokens
+  if (W) {  // logits of expert blockIdx.x for 16 tokens: all weight loads issued first
     const int e = blockIdx.x, t0 = blockIdx.y * kRTok;
     if (e < E) {
       const int nt = min(kRTok, T - t0);
@@ -206,17 +230,29 @@ __global__ void __launch_bounds__(256) decode_route_kernel(
 #pragma unroll
       for (int t = 0; t < kRTok; ++t) acc[t] = 0.f;
       const WT* w = W + (int64_t)e * H;
-      for (int h = tid * 4; h < H; h += 256 * 4) {
-        const float w0 = ldf(w + h), w1 = ldf(w + h + 1), w2 = ldf(w + h + 2), w3 = ldf(w + h + 3);
+      for (int h0 = 0; h0 < H; h0 += 4 * 1024) {
+        float wv[4][4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int h = h0 + (tid + 256 * j) * 4;
+          if (h < H) load4(w + h, wv[j]);
+          else wv[j][0] = wv[j][1] = wv[j][2] = wv[j][3] = 0.f;
+        }
 #pragma unroll
         for (int t = 0; t < kRTok; ++t) {
           if (t < nt) {
-            const uint2 xv = *reinterpret_cast<const uint2*>(x + (int64_t)(t0 + t) * H + h);
             float a = acc[t];
-            a = fmaf(bf16lo(xv.x), w0, a);
-            a = fmaf(bf16hi(xv.x), w1, a);
-            a = fmaf(bf16lo(xv.y), w2, a);
-            a = fmaf(bf16hi(xv.y), w3, a);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const int h = h0 + (tid + 256 * j) * 4;
+              if (h < H) {
+                const uint2 xv = *reinterpret_cast<const uint2*>(x + (int64_t)(t0 + t) * H + h);
+                a = fmaf(bf16lo(xv.x), wv[j][0], a);
+                a = fmaf(bf16hi(xv.x), wv[j][1], a);
+                a = fmaf(bf16lo(xv.y), wv[j][2], a);
+                a = fmaf(bf16hi(xv.y), wv[j][3], a);
+              }
+            }
             acc[t] = a;
           }
         }
@@ -239,73 +275,32 @@ __global__ void __launch_bounds__(256) decode_route_kernel(
       }
     }
   }
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) is_last = atomicAdd(&meta->ticket, 1u) == gridDim.x * gridDim.y - 1;
-  __syncthreads();
-  if (!is_last) return;
-  __threadfence();
-  if (W) {
-    for (int t = warp; t < T; t += 8)
-      warp_topk([&](int e2) { return __ldcg(logits + (int64_t)t * E + e2); }, E, k,
-                scores + (int64_t)t * k, idx + (int64_t)t * k);
-    __threadfence();
-    __syncthreads();
-  }
-  // dispatch: rows grouped by expert, (token, slot) order within an expert
-  const int n = T * k;
-  for (int e = tid; e < E; e += blockDim.x) cnt[e] = 0;
-  __syncthreads();
-  for (int i = tid; i < n; i += blockDim.x) {
-    const int e = __ldcg(idx + i);
-    if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
-    else record_status(status, BS_ERR_INVALID_ARGUMENT);
-  }
-  __syncthreads();
-  if (tid == 0) {
-    // groups: (expert | tokens << 16, first row), up to kGroupTok tokens each
-    int run = 0, ng = 0;
-    for (int e = 0; e < E; ++e) {
-      off[e] = run;
-      offsets[e] = run;
-      for (int c = 0; c < cnt[e]; c += kGroupTok) groups[ng++] = make_int2(e | (min(kGroupTok, cnt[e] - c) << 16), run + c);
-      run += cnt[e];
-    }
-    off[E] = run;
-    offsets[E] = run;
-    meta->n_groups = ng;
-  }
-  __syncthreads();
-  for (int i = tid; i < n; i += blockDim.x) {
-    const int e = __ldcg(idx + i);
-    if (e < 0 || e >= E) {
-      row_of_slot[i] = -1;
-      continue;
-    }
-    int r = 0;
-    for (int j = 0; j < i; ++j) r += (__ldcg(idx + j) == e);
-    const int pos = off[e] + r;
-    row_of_slot[i] = pos;
-    slot_of_row[pos] = i;
-  }
 }
 
 // ------------------------------------------------------------------ 2/3. experts
 struct MxArgs {
-  CUtensorMap tm_a;       // weight codes [E*Nw rows][K/2 bytes], box {128 B, 128 rows}, 128B swizzle
-  CUtensorMap tm_b;       // B term rows [rows][K/2 bytes], box {128 B, tokbox rows}, 128B swizzle
+  CUtensorMap tm_a;   // weight codes [E*Nw rows][K/2 bytes], box {128 B, 128 rows}, 128B swizzle
+  CUtensorMap tm_b;   // B term rows [R][K/2 bytes], box {128 B, nb rows}: a stage's tile or the tail chunk
+  CUtensorMap tm_b3;  // the same rows as {128 B, R rows, nfull chunks}, box {128, nb, nfull}
   const uint8_t* scales;  // [E][Nw][K/32] e8m0
   const void* bias;       // [E][Nw]
   int bias_f32;
   const uint8_t* bsf;     // B scales: rows (4 r + term) of gp bytes
   int gp;
-  const int2* groups;     // (expert | tokens << 16, first row) per group
-  const int* slot_of_row;
-  const DecodeMeta* meta;
-  const float* scores;
-  int E, Nw, K, k;
-  int nb;                 // B rows a stage holds (multiple of 16, >= 4 x tokens of any expert)
-  int stages, nsc, nacc;  // pipeline stages, per-item scale buffers, accumulator buffers
+  // routing: MODE 0 computes it (route_dispatch) and CTA 0 writes it out;
+  // MODE 1 reads it
+  const float* logits;    // [T][E] router logits, or NULL: idx / scores are the caller's
+  int32_t* idx;           // [T][k]
+  float* scores;          // [T][k]
+  int* offsets;           // [E + 1] first dispatch row of each expert
+  int* row_of_slot;       // [T k]
+  int* slot_of_row;       // [T k]
+  int2* groups;           // (expert | tokens << 16, first row) per group of an expert's tokens
+  DecodeMeta* meta;
+  int E, Nw, K, k, T;
+  int nb;                 // B rows of a tile (multiple of 16)
+  int b_mode;             // where B comes from: kBStage, kBItem, kBResident
+  int stages, nsc, nacc;  // pipeline stages, per-item buffers, accumulator buffers
   float alpha, limit;
   uint8_t* hq;            // MODE 0 out: rows (4 r + term) of Nw/4 bytes (codes of h, Nw/2 values)
   uint8_t* hs;            //             rows (4 r + term) of gp_out bytes
@@ -313,54 +308,203 @@ struct MxArgs {
   float* y;               // MODE 1 out: [rows][Nw] fp32
   int* status;
 };
+constexpr int kBStage = 0;     // one B tile per pipeline stage
+constexpr int kBItem = 1;      // an item's B tiles for all of K in one copy (per-item buffers)
+constexpr int kBResident = 2;  // MODE 0, few tokens: every token's B tiles and scales, loaded once
+constexpr int kBGather = 3;    // MODE 0, many tokens: the group's tokens' rows, one 4-row box each per stage
 
-// MODE 0: B rows are gathered per token (4 term rows each, one TMA box per
-// token); MODE 1: the expert's rows are contiguous (one box of nb rows).
+// Shared-memory plan of decode_mx_kernel (bytes; regions 1024-aligned).
+struct MxSmem {
+  int stage, ring_b, ring_sa, ring, res_b, res, total;
+};
+__host__ __device__ inline MxSmem mx_smem(int K, int nb, int b_mode, int gp, int S, int nsc) {
+  const int G = K / 32, nkc = (K + kKC - 1) / kKC;
+  auto al = [](int v) { return (v + 1023) & ~1023; };
+  MxSmem m;
+  m.stage = kBM * 128 + ((b_mode == kBStage || b_mode == kBGather) ? nb * 128 : 0);
+  m.ring_b = b_mode == kBItem ? nkc * nb * 128 : 0;        // B tiles of every chunk
+  m.ring_sa = (kBM * G + 15) & ~15;                         // A scale rows [128][G]
+  m.ring = al(m.ring_b + m.ring_sa + (b_mode == kBResident ? 0 : nb * gp));  // + B scale rows [nb][gp]
+  m.res_b = b_mode == kBResident ? nkc * nb * 128 : 0;
+  m.res = b_mode == kBResident ? al(m.res_b + nb * gp) : 0;
+  m.total = S * m.stage + nsc * m.ring + m.res + 1024;
+  return m;
+}
+
+// Top-k + softmax of every token (from the logits; modeling_gpt_oss.py:126-130)
+// and the dispatch (gptoss.py:143-154: rows grouped by expert, (token, slot)
+// order within an expert, groups of <= kGroupTok tokens), computed by every
+// CTA of the gate_up launch into shared memory -- the same result everywhere,
+// no cross-CTA handoff; CTA 0 writes it out for the later launches and the
+// caller.  `scratch` holds T k + E ints and, for the rank method, T E + T k floats.
+__device__ void route_dispatch(const MxArgs& p, int* scratch, int* s_slot, int2* s_grp, int* s_ngrp,
+                               int (*wsum)[2]) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int T = p.T, E = p.E, k = p.k, n = T * k;
+  const bool writer = blockIdx.x == 0;
+  int* s_idx = scratch;
+  int* cnt = scratch + n;
+  if (p.logits && T * E <= kRankMax) {
+    // rank every (token, expert): the number of experts ahead of it (higher
+    // logit, or equal and lower index; NaN counts as -inf); ranks < k are the
+    // top-k in order
+    float* lg = reinterpret_cast<float*>(scratch + n + E);
+    float* sv = lg + T * E;  // [T][k] selected logits
+    for (int i = tid; i < T * E; i += kThreads) {
+      const float v = __ldcg(p.logits + i);
+      lg[i] = v != v ? -INFINITY : v;
+    }
+    __syncthreads();
+    for (int i = tid; i < T * E; i += kThreads) {
+      const int t = i / E, e = i - t * E;
+      const float* row = lg + t * E;
+      const float v = row[e];
+      int r = 0;
+      for (int e2 = 0; e2 < E; ++e2) r += (row[e2] > v) | ((row[e2] == v) & (e2 < e));
+      if (r < k) {
+        s_idx[t * k + r] = e;
+        sv[t * k + r] = v;
+      }
+    }
+    __syncthreads();
+    if (writer)
+      for (int t = tid; t < T; t += kThreads) {
+        float sum = 0.f;
+        for (int j = 0; j < k; ++j) sum += expf(sv[t * k + j] - sv[t * k]);
+        for (int j = 0; j < k; ++j) p.scores[t * k + j] = expf(sv[t * k + j] - sv[t * k]) / sum;
+      }
+  } else if (p.logits) {
+    for (int t = warp; t < T; t += kThreads / 32)
+      warp_topk_any([&](int e2) { return __ldcg(p.logits + (int64_t)t * E + e2); }, E, k,
+                    writer ? p.scores + (int64_t)t * k : nullptr, s_idx + t * k);
+  } else {
+    for (int i = tid; i < n; i += kThreads) s_idx[i] = p.idx[i];
+  }
+  for (int e = tid; e < E; e += kThreads) cnt[e] = 0;
+  __syncthreads();
+  for (int i = tid; i < n; i += kThreads) {
+    const int e = s_idx[i];
+    if (writer && p.logits) p.idx[i] = e;
+    if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+    else if (writer) record_status(p.status, BS_ERR_INVALID_ARGUMENT);
+  }
+  __syncthreads();
+  // exclusive scans of rows and groups over the experts: threads 0-255, four each
+  int c[4], lc = 0, lg = 0, ic = 0, ig = 0;
+  if (tid < 256) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int e = tid * 4 + q;
+      c[q] = e < E ? cnt[e] : 0;
+      lc += c[q];
+      lg += (c[q] + kGroupTok - 1) / kGroupTok;
+    }
+    ic = lc, ig = lg;  // inclusive within the warp
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int uc = __shfl_up_sync(0xffffffffu, ic, o), ug = __shfl_up_sync(0xffffffffu, ig, o);
+      if (lane >= o) ic += uc, ig += ug;
+    }
+    if (lane == 31) wsum[warp][0] = ic, wsum[warp][1] = ig;
+  }
+  __syncthreads();
+  if (tid < 256) {
+    int rc = ic - lc, rg = ig - lg;
+    for (int w8 = 0; w8 < warp; ++w8) rc += wsum[w8][0], rg += wsum[w8][1];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int e = tid * 4 + q;
+      if (e < E) {
+        if (writer) p.offsets[e] = rc;
+        cnt[e] = rc;  // now the expert's first row
+        for (int c0 = 0; c0 < c[q]; c0 += kGroupTok) {
+          const int2 gr = make_int2(e | (min(kGroupTok, c[q] - c0) << 16), rc + c0);
+          s_grp[rg] = gr;
+          if (writer) p.groups[rg] = gr;
+          ++rg;
+        }
+        rc += c[q];
+      }
+      if (e == E - 1) {
+        *s_ngrp = rg;
+        if (writer) {
+          p.offsets[E] = rc;
+          p.meta->n_groups = rg;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  for (int i = tid; i < n; i += kThreads) {
+    const int e = s_idx[i];
+    if (e < 0 || e >= E) {
+      if (writer) p.row_of_slot[i] = -1;
+      continue;
+    }
+    int r = 0;
+    for (int j = 0; j < i; ++j) r += (s_idx[j] == e);
+    const int pos = cnt[e] + r;
+    s_slot[pos] = i;
+    if (writer) {
+      p.row_of_slot[i] = pos;
+      p.slot_of_row[pos] = i;
+    }
+  }
+  __syncthreads();
+}
+
+// MODE 0: B = the four term rows of tokens (every token's when resident or
+// per stage; the MMA computes them all and the epilogue keeps the expert's);
+// MODE 1: B = the group's own rows of h.
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_constant__ MxArgs p) {
   extern __shared__ uint8_t smem_raw[];
-  // data[s]: the stage's copies landed (TMA transaction count); empty[s]: the
-  // MMAs are done with it; scfull[b]: an item's scale rows landed in staging
-  // buffer b (one barrier per buffer, so a waiter is never two phases ahead);
-  // sfready[b]: its repacked scales are ready; accfull[b] / accempty[b]:
-  // accumulator handoff; drain: teardown
-  __shared__ uint64_t bars[3 * kMaxStages + 7];
+  // data[s] a stage's copies landed, empty[s] its MMAs are done, sffull[s] its
+  // scale factors are in TMEM; item[b] an item's scales (and B tiles) landed in
+  // ring buffer b, bfree[b] that item's MMAs are done; accfull / accempty:
+  // accumulator handoff; res: resident B landed; drain: teardown.  A waiter is
+  // never two phases ahead of a barrier it waits on.
+  __shared__ uint64_t bars[3 * kMaxStages + 2 * kMaxRing + 6];
   __shared__ uint32_t tmem_holder;
   __shared__ volatile int abort_flag;
   __shared__ float red[2][4][4];
   __shared__ int2 s_grp[kMaxGroups];  // (expert | tokens << 16, first row)
   __shared__ int s_ngrp;
+  __shared__ int s_slot[MODE == 0 ? kMaxDecodeT * 32 : 1];  // MODE 0: slot of each dispatch row
+  __shared__ int wsum[8][2];
   uint8_t* smem = smem_raw + ((1024u - (ptx::smem_addr(smem_raw) & 1023u)) & 1023u);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int S = p.stages;
-  const int K = p.K, G = K / 32, Nw = p.Nw;
-  const int a_bytes = kBM * 128, stage_bytes = a_bytes + p.nb * 128;
-  // per-item scale blocks (ring of p.nsc): A rows [128][G], B rows [nb][gp];
-  // then two buffers of repacked scales: per group q of four k-blocks, a
-  // 512-byte block for A and one for B (row r -> word (r % 32, r / 32))
-  const int sa_bytes = (kBM * G + 15) & ~15, sc_bytes = sa_bytes + p.nb * p.gp;
-  const int G4 = (G + 3) / 4;
-  const int sf_src_bytes = G4 * 1024;
-  uint8_t* scbuf = smem + S * stage_bytes;
-  uint8_t* sfsrc = scbuf + p.nsc * sc_bytes;
+  const int S = p.stages, NR = p.nsc;
+  const int K = p.K, G = K / 32, Nw = p.Nw, nb = p.nb;
+  const int nkc = (K + kKC - 1) / kKC, nfull = K / kKC;
+  const int nbk = nb > 128 ? 2 : 1;
+  const MxSmem L = mx_smem(K, nb, p.b_mode, p.gp, S, NR);
+  uint8_t* ring0 = smem + S * L.stage;
+  uint8_t* res = ring0 + NR * L.ring;
   auto data = [&](int s) { return ptx::smem_addr(bars + s); };
   auto empty = [&](int s) { return ptx::smem_addr(bars + kMaxStages + s); };
-  auto accfull = [&](int b) { return ptx::smem_addr(bars + 2 * kMaxStages + b); };
-  auto accempty = [&](int b) { return ptx::smem_addr(bars + 2 * kMaxStages + 2 + b); };
-  auto sfready = [&](int b) { return ptx::smem_addr(bars + 2 * kMaxStages + 4 + b); };
-  const uint32_t drain = ptx::smem_addr(bars + 2 * kMaxStages + 6);
-  auto scfull = [&](int b) { return ptx::smem_addr(bars + 2 * kMaxStages + 7 + b); };
+  auto sffull = [&](int s) { return ptx::smem_addr(bars + 2 * kMaxStages + s); };
+  auto itemb = [&](int b) { return ptx::smem_addr(bars + 3 * kMaxStages + b); };
+  auto bfree = [&](int b) { return ptx::smem_addr(bars + 3 * kMaxStages + kMaxRing + b); };
+  auto accfull = [&](int b) { return ptx::smem_addr(bars + 3 * kMaxStages + 2 * kMaxRing + b); };
+  auto accempty = [&](int b) { return ptx::smem_addr(bars + 3 * kMaxStages + 2 * kMaxRing + 2 + b); };
+  const uint32_t resb = ptx::smem_addr(bars + 3 * kMaxStages + 2 * kMaxRing + 4);
+  const uint32_t drain = ptx::smem_addr(bars + 3 * kMaxStages + 2 * kMaxRing + 5);
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       ptx::mbar_init(data(s), 1);
       ptx::mbar_init(empty(s), 1);
+      ptx::mbar_init(sffull(s), 4);
     }
-    for (int b = 0; b < p.nsc; ++b) ptx::mbar_init(scfull(b), 1);
+    for (int b = 0; b < NR; ++b) {
+      ptx::mbar_init(itemb(b), 1);
+      ptx::mbar_init(bfree(b), 1);
+    }
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(accfull(b), 1);
       ptx::mbar_init(accempty(b), 4);
-      ptx::mbar_init(sfready(b), 1);
     }
+    ptx::mbar_init(resb, 1);
     ptx::mbar_init(drain, 1);
     abort_flag = 0;
     ptx::fence_mbar_init();
@@ -372,70 +516,91 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
   if (warp == 4 && lane == 0) {
     ptx::tma_prefetch_desc(&p.tm_a);
     ptx::tma_prefetch_desc(&p.tm_b);
+    if (p.b_mode != kBStage && nfull > 0) ptx::tma_prefetch_desc(&p.tm_b3);
   }
-  pdl_wait();  // routing and the B operands come from the previous kernels
+  pdl_wait();  // the logits / routing and the B operands come from the previous kernels
   pdl_launch();
-  if (tid == 0) s_ngrp = p.meta->n_groups;
-  __syncthreads();
-  for (int i = tid; i < s_ngrp; i += kThreads) s_grp[i] = p.groups[i];
-  __syncthreads();
+  if (MODE == 0) {
+    // the stages' space is free until the pipeline starts
+    route_dispatch(p, reinterpret_cast<int*>(smem), s_slot, s_grp, &s_ngrp, wsum);
+  } else {
+    if (tid == 0) s_ngrp = p.meta->n_groups;
+    __syncthreads();
+    for (int i = tid; i < s_ngrp; i += kThreads) s_grp[i] = p.groups[i];
+    __syncthreads();
+  }
   ptx::tc_fence_after();
   const uint32_t tmem = tmem_holder;
 
   const int per_e = (Nw + kBM - 1) / kBM;
   const int n_items = s_ngrp * per_e;
-  const int nkc = (K + kKC - 1) / kKC;
   const int n_my = n_items > (int)blockIdx.x ? (n_items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
   const uint32_t smem0 = ptx::smem_addr(smem);
-  const uint32_t sf_base = (uint32_t)(p.nacc * p.nb);  // TMEM column of stage 0's scale factors
+  const uint32_t sf_base = (uint32_t)(p.nacc * nb);  // TMEM column of stage 0's scale factors
   auto item_of = [&](int it) { return (int)blockIdx.x + it * (int)gridDim.x; };
+  // B rows of an item: MODE 0 every token's (or, gathered, the group's
+  // tokens'), MODE 1 the group's
+  const bool gather = p.b_mode == kBGather;
+  auto brow0 = [&](int2 gr) { return MODE == 0 ? 0 : gr.y * kTerms; };
+  auto nbrows = [&](int2 gr) { return (MODE == 0 && !gather) ? kTerms * p.T : kTerms * (gr.x >> 16); };
 
   if (warp == 4) {
     // ---------------------------------------------------------- TMA producer (one thread)
     if (lane == 0) {
       int g = 0, n_issued = 0;
-      for (int it = 0; it < n_my; ++it) {
+      bool ok = true;
+      if (p.b_mode == kBResident && n_my > 0) {
+        // every token's B tiles and scale rows, once
+        const uint32_t rb = ptx::smem_addr(res);
+        ptx::mbar_arrive_expect_tx(resb, (uint32_t)(nkc * nb * 128 + kTerms * p.T * p.gp));
+        if (nfull > 0) ptx::tma_load_3d(rb, &p.tm_b3, resb, 0, 0, 0);
+        if (nfull < nkc) ptx::tma_load_2d(rb + nfull * nb * 128, &p.tm_b, resb, nfull * 128, 0);
+        ptx::bulk_load(rb + L.res_b, p.bsf, (uint32_t)(kTerms * p.T * p.gp), resb);
+      }
+      for (int it = 0; it < n_my && ok; ++it) {
         const int item = item_of(it);
         const int2 gr = s_grp[item / per_e];
-        const int e = gr.x & 0xFFFF, ntok = gr.x >> 16, row_lo = gr.y, r0 = (item % per_e) * kBM;
-        const int nrows = min(kBM, Nw - r0);
-        const uint32_t sca = ptx::smem_addr(scbuf + (it % p.nsc) * sc_bytes);
-        bool ok = true;
+        const int e = gr.x & 0xFFFF, r0 = (item % per_e) * kBM;
+        const int nrows = min(kBM, Nw - r0), nbv = nbrows(gr), b0 = brow0(gr);
+        const int b = it % NR;
+        if (it >= NR && !ptx::mbar_wait(bfree(b), ((it / NR) - 1) & 1, &abort_flag)) break;
+        const uint32_t sbt = ptx::smem_addr(ring0 + b * L.ring), sca = sbt + L.ring_b, scb = sca + L.ring_sa;
+        // the item's scale rows (A contiguous [rows][G], B [nbv][gp]) and, per
+        // item, its B tiles for all of K
+        uint32_t tx = nrows * G;
+        if (p.b_mode != kBResident) tx += nbv * p.gp;
+        if (p.b_mode == kBItem) tx += nkc * nb * 128;
+        ptx::mbar_arrive_expect_tx(itemb(b), tx);
+        ptx::bulk_load(sca, p.scales + ((int64_t)e * Nw + r0) * G, (uint32_t)(nrows * G), itemb(b));
+        if (gather) {
+          for (int j = 0; j < (gr.x >> 16); ++j)
+            ptx::bulk_load(scb + j * kTerms * p.gp, p.bsf + (int64_t)(s_slot[gr.y + j] / p.k) * kTerms * p.gp,
+                           (uint32_t)(kTerms * p.gp), itemb(b));
+        } else if (p.b_mode != kBResident) {
+          ptx::bulk_load(scb, p.bsf + (int64_t)b0 * p.gp, (uint32_t)(nbv * p.gp), itemb(b));
+        }
+        if (p.b_mode == kBItem) {
+          if (nfull > 0) ptx::tma_load_3d(sbt, &p.tm_b3, itemb(b), 0, b0, 0);
+          if (nfull < nkc) ptx::tma_load_2d(sbt + nfull * nb * 128, &p.tm_b, itemb(b), nfull * 128, b0);
+        }
+        ++n_issued;
         for (int kc = 0; kc < nkc; ++kc, ++g) {
           const int s = g % S;
           if (g >= S && !ptx::mbar_wait(empty(s), ((g / S) - 1) & 1, &abort_flag)) {
             ok = false;
             break;
           }
-          const uint32_t sa = smem0 + s * stage_bytes, sb = sa + a_bytes;
-          if (kc == 0) {
-            // the item's scale rows: A contiguous [rows][G], B [4 x tokens][gp]
-            const uint32_t scb = scfull(it % p.nsc);
-            ptx::mbar_arrive_expect_tx(scb, (uint32_t)(nrows * G + ntok * kTerms * p.gp));
-            ptx::bulk_load(sca, p.scales + ((int64_t)e * Nw + r0) * G, (uint32_t)(nrows * G), scb);
-            if (MODE == 0) {
-              for (int j = 0; j < ntok; ++j) {
-                const int t = p.slot_of_row[row_lo + j] / p.k;
-                ptx::bulk_load(sca + sa_bytes + j * kTerms * p.gp, p.bsf + (int64_t)t * kTerms * p.gp,
-                               (uint32_t)(kTerms * p.gp), scb);
-              }
-            } else {
-              ptx::bulk_load(sca + sa_bytes, p.bsf + (int64_t)row_lo * kTerms * p.gp,
-                             (uint32_t)(ntok * kTerms * p.gp), scb);
-            }
-            ++n_issued;
-          }
-          ptx::mbar_arrive_expect_tx(data(s), a_bytes + (MODE == 0 ? ntok * kTerms * 128 : p.nb * 128));
+          const uint32_t sa = smem0 + s * L.stage;
+          ptx::mbar_arrive_expect_tx(data(s), (uint32_t)(gather ? kBM * 128 + nbv * 128 : L.stage));
           ptx::tma_load_2d(sa, &p.tm_a, data(s), kc * 128, e * Nw + r0);
-          if (MODE == 0) {
-            for (int j = 0; j < ntok; ++j)
-              ptx::tma_load_2d(sb + j * kTerms * 128, &p.tm_b, data(s), kc * 128,
-                               (p.slot_of_row[row_lo + j] / p.k) * kTerms);
-          } else {
-            ptx::tma_load_2d(sb, &p.tm_b, data(s), kc * 128, row_lo * kTerms);
+          if (p.b_mode == kBStage) ptx::tma_load_2d(sa + kBM * 128, &p.tm_b, data(s), kc * 128, b0);
+          if (gather) {
+            // one 4-row box per token of the group (the stage's count covers exactly these)
+            for (int j = 0; j < (gr.x >> 16); ++j)
+              ptx::tma_load_2d(sa + kBM * 128 + j * kTerms * 128, &p.tm_b, data(s), kc * 128,
+                               (s_slot[gr.y + j] / p.k) * kTerms);
           }
         }
-        if (!ok) break;
       }
       if (abort_flag) {
         // after a timeout elsewhere: let this CTA's copies in flight land
@@ -443,8 +608,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
         volatile int quiet = 0;
         for (int gg = max(0, g - S); gg < g; ++gg)
           ptx::mbar_wait(data(gg % S), (gg / S) & 1, &quiet, 100000000LL);
-        for (int it2 = max(0, n_issued - p.nsc); it2 < n_issued; ++it2)
-          ptx::mbar_wait(scfull(it2 % p.nsc), (it2 / p.nsc) & 1, &quiet, 100000000LL);
+        for (int i2 = max(0, n_issued - NR); i2 < n_issued; ++i2)
+          ptx::mbar_wait(itemb(i2 % NR), (i2 / NR) & 1, &quiet, 100000000LL);
+        if (p.b_mode == kBResident && n_my > 0) ptx::mbar_wait(resb, 0, &quiet, 100000000LL);
       }
     }
     __syncwarp();
@@ -453,93 +619,124 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
     if (lane == 0) {
       int g = 0;
       bool ok = true;
+      if (p.b_mode == kBResident && n_my > 0) ok = ptx::mbar_wait(resb, 0, &abort_flag);
       for (int it = 0; it < n_my && ok; ++it) {
         const int item = item_of(it);
-        const int ntok = s_grp[item / per_e].x >> 16;
-        const int N = ((kTerms * ntok + 15) / 16) * 16;
-        const int ab = it % p.nacc;
-        if (!ptx::mbar_wait(sfready(it & 1), (it >> 1) & 1, &abort_flag)) break;
-        if (it >= p.nacc) {
-          if (!ptx::mbar_wait(accempty(ab), ((it / p.nacc) - 1) & 1, &abort_flag)) break;
-        }
+        const int2 gr = s_grp[item / per_e];
+        const int N = ((nbrows(gr) + 15) / 16) * 16;
+        const int ab = it % p.nacc, b = it % NR;
+        if (it >= p.nacc && !ptx::mbar_wait(accempty(ab), ((it / p.nacc) - 1) & 1, &abort_flag)) break;
+        if (p.b_mode == kBItem && !ptx::mbar_wait(itemb(b), (it / NR) & 1, &abort_flag)) break;
         ptx::tc_fence_after();
-        const uint32_t acc = tmem + ab * p.nb;
-        const uint32_t src = ptx::smem_addr(sfsrc + (it & 1) * sf_src_bytes);
+        const uint32_t acc = tmem + ab * nb;
+        const uint32_t bt = p.b_mode == kBItem ? ptx::smem_addr(ring0 + b * L.ring) : ptx::smem_addr(res);
         for (int kc = 0; kc < nkc; ++kc, ++g) {
           const int s = g % S;
-          if (!ptx::mbar_wait(data(s), (g / S) & 1, &abort_flag)) {
+          if (!ptx::mbar_wait(data(s), (g / S) & 1, &abort_flag) ||
+              !ptx::mbar_wait(sffull(s), (g / S) & 1, &abort_flag)) {
             ok = false;
             break;
           }
           ptx::tc_fence_after();
-          const uint32_t sa = smem0 + s * stage_bytes;
-          const uint64_t ad = ptx::sdesc_kmajor_sw128(sa), bd = ptx::sdesc_kmajor_sw128(sa + a_bytes);
+          const uint32_t sa = smem0 + s * L.stage;
+          const uint64_t ad = ptx::sdesc_kmajor_sw128(sa);
+          const uint64_t bd = ptx::sdesc_kmajor_sw128((p.b_mode == kBStage || gather) ? sa + kBM * 128
+                                                                                      : bt + kc * nb * 128);
+          // scale factors (written by warps 6-9): SFA at columns 4q, SFB at
+          // 8 + 4 nbk q for groups q = 0, 1 of four k-blocks
           const uint32_t sf = tmem + sf_base + s * kSfStageCols;
-          // the stage's scale factors: groups 2 kc, 2 kc + 1 of four k-blocks;
-          // SFA at columns 4q, SFB at 8 + 4q
-          for (int q = 0; q < 2 && 4 * (2 * kc + q) < G; ++q) {
-            const int gq = 2 * kc + q;
-            ptx::tc_cp_32x128b_warpx4(sf + 4 * q, ptx::sdesc_rows16(src + gq * 512));
-            ptx::tc_cp_32x128b_warpx4(sf + 8 + 4 * q, ptx::sdesc_rows16(src + (G4 + gq) * 512));
-          }
           for (int i = 0; i < 4 && kc * kKC + i * 64 < K; ++i) {
             const uint32_t id = 2 * (i & 1);
             ptx::mma_mxf4_ss(acc, ad + 2 * i, bd + 2 * i, ptx::idesc_mxf4(N, id, id), sf + 4 * (i >> 1),
-                             sf + 8 + 4 * (i >> 1), (kc | i) != 0);
+                             sf + 8 + 4 * nbk * (i >> 1), (kc | i) != 0);
           }
           ptx::tc_commit(empty(s));
         }
-        if (ok) ptx::tc_commit(accfull(ab));
+        if (ok) {
+          ptx::tc_commit(accfull(ab));
+          ptx::tc_commit(bfree(b));
+        }
       }
     }
     __syncwarp();
-  } else {
-    // ---------------------------------------------------------- scale factors + epilogue
-    const uint32_t lanes = (uint32_t)(32 * warp) << 16;
+  } else if (warp >= 6) {
+    // ---------------------------------------------------------- scale factors into TMEM
+    // This warp writes its own 32-lane subpartition; the four hold copies.
+    // SFA word (q, j) of lane l: scales of row l + 32 j, k-blocks 4q..4q+3;
+    // SFB word (q, j): B row l + 32 j.
+    const uint32_t lanes = (uint32_t)(32 * (warp & 3)) << 16;
+    int g = 0;
     bool ok = true;
-    // repack item `it`'s scales (landed with its first stage) into the blocks
-    // tcgen05.cp reads; the MMA thread copies them into TMEM stage by stage
-    auto repack = [&](int it) {
+    if (p.b_mode == kBResident && n_my > 0) {
+      bool w = true;
+      if (lane == 0) w = ptx::mbar_wait(resb, 0, &abort_flag);
+      ok = __shfl_sync(0xffffffffu, w, 0);
+    }
+    for (int it = 0; it < n_my && ok; ++it) {
       const int item = item_of(it);
       const int2 gr = s_grp[item / per_e];
       const int r0 = (item % per_e) * kBM;
-      const int nrows = min(kBM, Nw - r0);
-      const int nbv = kTerms * (gr.x >> 16);
+      const int nrows = min(kBM, Nw - r0), nbv = nbrows(gr);
+      const int b = it % NR;
       bool w = true;
-      if (lane == 0) w = ptx::mbar_wait(scfull(it % p.nsc), (it / p.nsc) & 1, &abort_flag);
-      if (!named_and(2, 128, __shfl_sync(0xffffffffu, w, 0))) {
-        ok = false;
-        return;
-      }
-      const uint8_t* sca = scbuf + (it % p.nsc) * sc_bytes;
-      const uint8_t* scb = sca + sa_bytes;
-      uint8_t* dst = sfsrc + (it & 1) * sf_src_bytes;
-      {
-        // A: thread r = row; rows are 2-byte aligned runs of G bytes
-        const int r = tid;
-        const uint16_t* row = reinterpret_cast<const uint16_t*>(sca + r * G);
-        for (int q = 0; q < G4; ++q) {
-          uint32_t v = 0;
-          if (r < nrows) v = row[2 * q] | ((4 * q + 2 < G) ? (uint32_t)row[2 * q + 1] << 16 : 0u);
-          *reinterpret_cast<uint32_t*>(dst + q * 512 + (r & 31) * 16 + (r >> 5) * 4) = v;
+      if (lane == 0) w = ptx::mbar_wait(itemb(b), (it / NR) & 1, &abort_flag);
+      if (!__shfl_sync(0xffffffffu, w, 0)) break;
+      const uint8_t* sca = ring0 + b * L.ring + L.ring_b;
+      const uint8_t* scb = p.b_mode == kBResident ? res + L.res_b : sca + L.ring_sa;
+      for (int kc = 0; kc < nkc; ++kc, ++g) {
+        const int s = g % S;
+        if (g >= S) {
+          if (lane == 0) w = ptx::mbar_wait(empty(s), ((g / S) - 1) & 1, &abort_flag);
+          if (!__shfl_sync(0xffffffffu, w, 0)) {
+            ok = false;
+            break;
+          }
         }
+        uint32_t wa[8], wb[16];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const int gq = 2 * kc + q;
+          const bool gv = 4 * gq < G;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int r = lane + 32 * j;
+            uint32_t v = 0;
+            if (gv && r < nrows) {
+              const uint16_t* row = reinterpret_cast<const uint16_t*>(sca + r * G);
+              v = row[2 * gq] | ((4 * gq + 2 < G) ? (uint32_t)row[2 * gq + 1] << 16 : 0u);
+            }
+            wa[4 * q + j] = v;
+          }
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int r = lane + 32 * j;
+            const uint32_t u = (gv && j < 4 * nbk && r < nbv) ? *reinterpret_cast<const uint32_t*>(scb + r * p.gp + 4 * gq) : 0u;
+            if (nbk == 1) {
+              if (j < 4) wb[4 * q + j] = u;
+            } else {
+              wb[8 * q + j] = u;
+            }
+          }
+        }
+        const uint32_t sf = tmem + lanes + sf_base + s * kSfStageCols;
+        ptx::tmem_st_32x32b_x8(sf, wa);
+        if (nbk == 1) ptx::tmem_st_32x32b_x8(sf + 8, wb);
+        else ptx::tmem_st_32x32b_x16(sf + 8, wb);
+        ptx::tmem_wait_st();
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(sffull(s));
       }
-      // B: rows n < nbv (pitch gp, 16-byte aligned words)
-      for (int idx = tid; idx < nbv * G4; idx += 128) {
-        const int n = idx / G4, q = idx - n * G4;
-        const uint32_t v = *reinterpret_cast<const uint32_t*>(scb + n * p.gp + 4 * q);
-        *reinterpret_cast<uint32_t*>(dst + (G4 + q) * 512 + (n & 31) * 16 + (n >> 5) * 4) = v;
-      }
-      ptx::fence_proxy_async_smem();
-      named_sync(2, 128);
-      if (tid == 0) ptx::mbar_arrive(sfready(it & 1));
-    };
-    auto epilogue = [&](int it) {
+    }
+  } else {
+    // ---------------------------------------------------------- epilogue
+    const uint32_t lanes = (uint32_t)(32 * warp) << 16;
+    bool ok = true;
+    for (int it = 0; it < n_my && ok; ++it) {
       const int item = item_of(it);
       const int2 gr = s_grp[item / per_e];
       const int e = gr.x & 0xFFFF, ntok = gr.x >> 16, row_lo = gr.y, r0 = (item % per_e) * kBM;
       const int nrows = min(kBM, Nw - r0);
-      const int N = ((kTerms * ntok + 15) / 16) * 16;
       const int ab = it % p.nacc;
       const int lrow = 32 * warp + lane;
       const bool rv = lrow < nrows;
@@ -548,43 +745,43 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
       if (rv && p.bias)
         bv = p.bias_f32 ? static_cast<const float*>(p.bias)[grow]
                         : __bfloat162float(static_cast<const __nv_bfloat16*>(p.bias)[grow]);
-      float wt0 = 0.f, wt1 = 0.f;  // MODE 1: routing weights of tokens lane, lane + 32
-      if (MODE == 1) {
-        if (lane < ntok) wt0 = p.scores[p.slot_of_row[row_lo + lane]];
-        if (lane + 32 < ntok) wt1 = p.scores[p.slot_of_row[row_lo + lane + 32]];
+      // per token j of the group: its accumulator column (MODE 0: the token's
+      // row among all tokens) and, MODE 1, its routing weight
+      int col = 0;
+      float wt = 0.f;
+      if (lane < ntok) {
+        const int sl = MODE == 0 ? s_slot[row_lo + lane] : p.slot_of_row[row_lo + lane];
+        col = (MODE == 0 && !gather) ? kTerms * (sl / p.k) : kTerms * lane;
+        if (MODE == 1) wt = p.scores[sl];
       }
-      bool got = ok;
-      if (got) got = ptx::mbar_wait(accfull(ab), (it / p.nacc) & 1, &abort_flag);
-      if (!named_and(1, 128, got)) {
-        ok = false;
-        return;
-      }
+      bool got = ptx::mbar_wait(accfull(ab), (it / p.nacc) & 1, &abort_flag);
+      if (!named_and(1, 128, got)) break;
       ptx::tc_fence_after();
-      const uint32_t tl = tmem + lanes + ab * p.nb;
-      for (int c = 0; c < N / 16; ++c) {
-        float v[16];
-        {
-          uint32_t u[16];
-          ptx::tmem_ld_32x32b_x16(tl + c * 16, u);
-          ptx::tmem_wait_ld();
+      const uint32_t tl = tmem + lanes + ab * nb;
+      const int nchunk = (ntok + 3) / 4;
+      for (int c = 0; c < nchunk; ++c) {
+        float acc[4];
 #pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(u[j]);
+        for (int jj = 0; jj < 4; ++jj) {
+          const int cj = __shfl_sync(0xffffffffu, col, (c * 4 + jj) & 31);
+          uint32_t u[4];
+          ptx::tmem_ld_32x32b_x4(tl + cj, u);  // tokens past ntok read column 0, unused
+          ptx::tmem_wait_ld();
+          acc[jj] = __uint_as_float(u[0]) + __uint_as_float(u[1]) + __uint_as_float(u[2]) +
+                    __uint_as_float(u[3]) + bv;
         }
-        if (c == N / 16 - 1) {
+        if (c == nchunk - 1) {
           // accumulator drained: the MMAs of a later item may use it
           ptx::tc_fence_before();
           __syncwarp();
           if (lane == 0) ptx::mbar_arrive(accempty(ab));
         }
-        float acc[4];
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) acc[jj] = v[4 * jj] + v[4 * jj + 1] + v[4 * jj + 2] + v[4 * jj + 3] + bv;
         if (MODE == 1) {
 #pragma unroll
           for (int jj = 0; jj < 4; ++jj) {
             const int tok = c * 4 + jj;
-            const float wt = __shfl_sync(0xffffffffu, tok < 32 ? wt0 : wt1, tok & 31);
-            if (tok < ntok && rv) p.y[(int64_t)(row_lo + tok) * Nw + r0 + lrow] = acc[jj] * wt;
+            const float w = __shfl_sync(0xffffffffu, wt, tok & 31);
+            if (tok < ntok && rv) p.y[(int64_t)(row_lo + tok) * Nw + r0 + lrow] = acc[jj] * w;
           }
         } else {
           // rows alternate gate / up: h_i (i = row / 2) sits in lanes 2m, 2m+1;
@@ -623,23 +820,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
           }
         }
       }
-    };
-    // The epilogue of item it-1 runs after the repack of item it when two
-    // accumulators alternate (the MMAs of item it overlap it); with one,
-    // item it's MMAs need that epilogue first.
-    for (int it = 0; it < n_my && ok; ++it) {
-      if (p.nacc == 1 && it > 0) epilogue(it - 1);
-      if (!ok) break;
-      repack(it);
-      if (p.nacc == 2 && it > 0 && ok) epilogue(it - 1);
     }
-    if (ok && n_my > 0) epilogue(n_my - 1);
   }
   __syncthreads();
   if (warp == 5) {
     if (lane == 0 && abort_flag) {
-      // MMAs and copies may still be in flight after a timeout: let the MMAs
-      // finish (bounded) before the tensor memory is released.
+      // MMAs may still be in flight after a timeout: let them finish (bounded)
+      // before the tensor memory is released.
       record_status(p.status, BS_ERR_TIMEOUT);
       ptx::tc_commit(drain);
       volatile int quiet = 0;
@@ -692,22 +879,22 @@ int launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t st, A
 // Pitch of a row of per-32 scales (16-byte multiple: rows are bulk-copied).
 int gp_of(int64_t K) { return (int)align_up((size_t)(K / 32), 16); }
 
-// Pipeline shape of one expert projection: stages, scale buffers and
-// accumulator buffers that fit in shared and tensor memory.
-int plan_mx(MxArgs& a) {
-  const int64_t K = a.K, G = K / 32, nkc = cdiv(K, (int64_t)kKC);
-  const size_t stage = (size_t)(kBM + a.nb) * 128;
-  const size_t sc = align_up((size_t)kBM * G, 16) + (size_t)a.nb * a.gp;
-  const size_t a4 = 2 * (size_t)cdiv(G, (int64_t)4) * 1024;  // repacked scales
-  const size_t budget = 200 * 1024;  // dynamic shared memory (the static arrays take ~9 KB)
+// Pipeline shape of one expert projection: where B comes from, stages,
+// per-item buffers and accumulator buffers that fit in shared and tensor
+// memory.  Resident B (MODE 0, few tokens) or per-item B when that leaves at
+// least four stages; else a B tile per stage.
+int plan_mx(MxArgs& a, std::initializer_list<int> modes) {
+  const int budget = 198 * 1024;  // dynamic shared memory (the static arrays take ~18 KB)
   a.stages = 0;
-  for (int S = kMaxStages; S >= 2; --S) {
-    const int nsc = (int)std::max<int64_t>(2, cdiv((int64_t)S - 1, nkc) + 1);
-    if (S * stage + nsc * sc + a4 + 1024 <= budget) {
-      a.stages = S;
-      a.nsc = nsc;
-      break;
+  for (int b_mode : modes) {
+    for (int S = kMaxStages; S >= ((b_mode == kBStage || b_mode == kBGather) ? 2 : 4); --S) {
+      const int nsc = 2;
+      if (mx_smem(a.K, a.nb, b_mode, a.gp, S, nsc).total <= budget) {
+        a.b_mode = b_mode, a.stages = S, a.nsc = nsc;
+        break;
+      }
     }
+    if (a.stages) break;
   }
   BS_REQUIRE(a.stages >= 2, BS_ERR_UNSUPPORTED, "decode path: B tile of %d rows does not fit", a.nb);
   a.nacc = (2 * a.nb + a.stages * kSfStageCols <= kTmemCols) ? 2 : 1;
@@ -716,17 +903,25 @@ int plan_mx(MxArgs& a) {
   return BS_OK;
 }
 
-size_t mx_smem_bytes(const MxArgs& a) {
-  const int64_t G = a.K / 32;
-  const size_t stage = (size_t)(kBM + a.nb) * 128;
-  const size_t sc = align_up((size_t)kBM * G, 16) + (size_t)a.nb * a.gp;
-  const size_t a4 = 2 * (size_t)cdiv(G, (int64_t)4) * 1024;
-  return a.stages * stage + a.nsc * sc + a4 + 1024;
+// Maps of B: per-stage / tail boxes of nb rows, and the item's full chunks in one 3-D box.
+int make_b_maps(MxArgs& a, const void* rows_base, int64_t rows) {
+  const CUtensorMapDataType u8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B;
+  const int64_t pitch = a.K / 2, nfull = a.K / kKC;
+  const uint32_t box_rows = a.b_mode == kBGather ? kTerms : (uint32_t)a.nb;
+  BS_TRY(make_map_2d(&a.tm_b, u8, rows_base, (uint64_t)pitch, (uint64_t)rows, (uint64_t)pitch, 128, box_rows, sw));
+  if (a.b_mode != kBStage && nfull > 0) {
+    const uint64_t dims[3] = {128, (uint64_t)rows, (uint64_t)nfull};
+    const uint64_t strides[2] = {(uint64_t)pitch, 128};
+    const uint32_t box[3] = {128, (uint32_t)a.nb, (uint32_t)nfull};
+    BS_TRY(make_map_3d(&a.tm_b3, u8, rows_base, dims, strides, box, sw));
+  }
+  return BS_OK;
 }
 
 template <int MODE>
 int launch_mx(const MxArgs& a, cudaStream_t st) {
-  const size_t smem = mx_smem_bytes(a);
+  const size_t smem = mx_smem(a.K, a.nb, a.b_mode, a.gp, a.stages, a.nsc).total;
   BS_CUDA(cudaFuncSetAttribute(decode_mx_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   return launch_pdl(decode_mx_kernel<MODE>, dim3((unsigned)sm_count()), dim3(kThreads), smem, st, a);
 }
@@ -793,39 +988,39 @@ int decode_forward(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, in
              BS_ERR_MISALIGNED, "decode path: expert blocks and scales must be 16-byte aligned");
   const DecodeWS w = decode_carve(ws, T, H, I, E, k);
   int* status = device_status_ptr();
-  BS_CUDA(cudaMemsetAsync(w.meta, 0, sizeof(DecodeMeta), st));
   const int64_t G = H / 32;
   const dim3 rgrid((unsigned)std::max<int64_t>(rw ? E : 1, std::min<int64_t>(G, 128)),
                    (unsigned)cdiv(T, (int64_t)kRTok));
   if (!rw || rdt == BS_F32) {
     BS_TRY(launch_pdl(decode_route_kernel<float>, rgrid, dim3(256), 0, st,
                       static_cast<const __nv_bfloat16*>(x), static_cast<const float*>(rw),
-                      static_cast<const float*>(rb), (int)T, (int)H, (int)E, (int)k, 0, w.logits,
-                      scores, indices, w.offsets, w.row_of_slot, w.slot_of_row, w.groups, w.xq, w.xs,
-                      gp_of(H), w.meta, status));
+                      static_cast<const float*>(rb), (int)T, (int)H, (int)E, 0, w.logits, w.xq, w.xs,
+                      gp_of(H)));
   } else {
     BS_TRY(launch_pdl(decode_route_kernel<__nv_bfloat16>, rgrid, dim3(256), 0, st,
                       static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(rw),
-                      static_cast<const __nv_bfloat16*>(rb), (int)T, (int)H, (int)E, (int)k, 1,
-                      w.logits, scores, indices, w.offsets, w.row_of_slot, w.slot_of_row, w.groups,
-                      w.xq, w.xs, gp_of(H), w.meta, status));
+                      static_cast<const __nv_bfloat16*>(rb), (int)T, (int)H, (int)E, 1, w.logits, w.xq,
+                      w.xs, gp_of(H)));
   }
-  const int nb = (int)((std::min<int64_t>(kTerms * T, kTerms * kGroupTok) + 15) / 16 * 16);
   MxArgs a{};
-  a.groups = w.groups;
-  a.slot_of_row = w.slot_of_row;
-  a.meta = w.meta;
+  a.logits = rw ? w.logits : nullptr;
+  a.idx = indices;
   a.scores = scores;
+  a.offsets = w.offsets;
+  a.row_of_slot = w.row_of_slot;
+  a.slot_of_row = w.slot_of_row;
+  a.groups = w.groups;
+  a.meta = w.meta;
   a.E = (int)E;
   a.k = (int)k;
-  a.nb = nb;
+  a.T = (int)T;
   a.alpha = alpha;
   a.limit = limit;
   a.bias_f32 = bias_f32;
   a.status = status;
   const CUtensorMapDataType u8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
   const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B;
-  // gate_up: A = [E][2I][H/32][16], B = x terms (4 rows per token), out = h terms
+  // gate_up: A = [E][2I][H/32][16], B = x terms of every token, out = h terms
   a.scales = static_cast<const uint8_t*>(gu_s);
   a.bias = gu_bias;
   a.bsf = w.xs;
@@ -836,9 +1031,14 @@ int decode_forward(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, in
   a.hs = w.hs;
   a.gp_out = gp_of(I);
   BS_TRY(make_map_2d(&a.tm_a, u8, gu_b, (uint64_t)(H / 2), (uint64_t)(E * 2 * I), (uint64_t)(H / 2), 128, kBM, sw));
-  BS_TRY(make_map_2d(&a.tm_b, u8, w.xq, (uint64_t)(H / 2), (uint64_t)(T * kTerms), (uint64_t)(H / 2), 128,
-                     kTerms, sw));
-  BS_TRY(plan_mx(a));
+  if (T <= kGroupTok) {  // every token's terms as B
+    a.nb = (int)((kTerms * T + 15) / 16 * 16);
+    BS_TRY(plan_mx(a, {kBResident, kBStage}));
+  } else {  // the group's tokens' terms, gathered
+    a.nb = kTerms * kGroupTok;
+    BS_TRY(plan_mx(a, {kBGather}));
+  }
+  BS_TRY(make_b_maps(a, w.xq, T * kTerms));
   BS_TRY(launch_mx<0>(a, st));
   // down: A = [E][H][I/32][16], B = h terms (contiguous per expert), out = weighted fp32 rows
   a.scales = static_cast<const uint8_t*>(dn_s);
@@ -849,9 +1049,9 @@ int decode_forward(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, in
   a.K = (int)I;
   a.y = w.y;
   BS_TRY(make_map_2d(&a.tm_a, u8, dn_b, (uint64_t)(I / 2), (uint64_t)(E * H), (uint64_t)(I / 2), 128, kBM, sw));
-  BS_TRY(make_map_2d(&a.tm_b, u8, w.hq, (uint64_t)(I / 2), (uint64_t)(T * k * kTerms), (uint64_t)(I / 2), 128,
-                     (uint32_t)nb, sw));
-  BS_TRY(plan_mx(a));
+  a.nb = (int)((kTerms * std::min<int64_t>(T, kGroupTok) + 15) / 16 * 16);  // a group's tokens
+  BS_TRY(plan_mx(a, {kBItem, kBStage}));
+  BS_TRY(make_b_maps(a, w.hq, T * k * kTerms));
   BS_TRY(launch_mx<1>(a, st));
   const int vecs = (int)(H / 4);
   const int cgrid = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(T * vecs, (int64_t)256), sm_count() * 4));
