@@ -18,24 +18,30 @@
 //
 // The layer runs as four launches chained with programmatic dependent launch:
 //  1. decode_route_kernel  x -> four e2m1 terms; router logits with one CTA per
-//     (expert, 16 tokens) (modeling_gpt_oss.py:126-130); the last CTA to finish
-//     (ticket counter) runs top-k + softmax over the k and the dispatch
-//     (gptoss.py:143-154) and writes the list of experts that received tokens.
-//  2. decode_mx_kernel<0>  gate_up + bias + clamped SwiGLU (gptoss.py:130-135,
-//     158-166); h is written as four e2m1 terms for the next projection.
+//     (expert, 16 tokens) (modeling_gpt_oss.py:126-130).
+//  2. decode_mx_kernel<0>  every CTA first computes top-k + softmax over the k
+//     (modeling_gpt_oss.py:126-130) and the dispatch (gptoss.py:143-154) into
+//     its shared memory, CTA 0 writing them out; then gate_up + bias +
+//     clamped SwiGLU (gptoss.py:130-135, 158-166); h is written as four e2m1
+//     terms for the next projection.
 //  3. decode_mx_kernel<1>  down + bias, times the routing weight (167-175),
 //     fp32 rows.
 //  4. decode_combine_kernel out[t] = bf16(sum over the k slots), fp32 sum.
 //
 // Work item of 2/3: 128 weight rows of one expert and a group of up to 16 of
-// its tokens (the route kernel lists the groups).  One CTA per SM: warp 4
-// issues the TMA copies (weight tiles [128 rows x 256 codes] as stored, the B
-// term rows, per-item scale blocks), warp 5 the MMAs, warps 6-9 (one per
-// 32-lane TMEM subpartition) write every stage's scale factors into TMEM with
-// tcgen05.st, warps 0-3 drain the accumulators.  On this GPU each
-// tcgen05.mma, tcgen05.cp and tcgen05.commit takes ~100 cycles of the tensor
-// pipe, so the scale factors stay out of it: the pipe runs 4 MMAs + 1 commit
-// per 16 KB stage, less than the stage's HBM time.
+// its tokens.  One CTA per SM: warp 4 issues the TMA copies (weight tiles
+// [128 rows x 256 codes] as stored, the B term rows, per-item scale blocks),
+// warp 5 the MMAs, warps 6-9 (one per 32-lane TMEM subpartition) write every
+// stage's scale factors into TMEM with tcgen05.st, warps 0-3 drain the
+// accumulators.  On this GPU each tcgen05.mma, tcgen05.cp and tcgen05.commit
+// takes ~100 cycles of the tensor pipe, so the scale factors stay out of it:
+// the pipe runs 4 MMAs + 1 commit per 16 KB stage, less than the stage's HBM
+// time.
+//
+// Measured here: code that runs once per item (epilogue, routing) executes
+// with a cold instruction cache while the weights saturate HBM, where each
+// fetch of a few instructions waits on the memory system; such code is kept
+// short and in loops rather than unrolled where its latency is exposed.
 #include "bs_common.cuh"
 #include "bs_ptx.cuh"
 
@@ -457,8 +463,11 @@ __device__ void route_dispatch(const MxArgs& p, int* scratch, int* s_slot, int2*
 // per stage; the MMA computes them all and the epilogue keeps the expert's);
 // MODE 1: B = the group's own rows of h.
 template <int MODE>
-__global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_constant__ MxArgs p) {
+__global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_constant__ MxArgs pa) {
   extern __shared__ uint8_t smem_raw[];
+  // The roles read the arguments from a shared-memory copy; the tensor maps
+  // stay in parameter space for the TMA unit.
+  __shared__ MxArgs p;
   // data[s] a stage's copies landed, empty[s] its MMAs are done, sffull[s] its
   // scale factors are in TMEM; item[b] an item's scales (and B tiles) landed in
   // ring buffer b, bfree[b] that item's MMAs are done; accfull / accempty:
@@ -474,6 +483,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
   __shared__ int wsum[8][2];
   uint8_t* smem = smem_raw + ((1024u - (ptx::smem_addr(smem_raw) & 1023u)) & 1023u);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  {
+    static_assert(sizeof(MxArgs) % 16 == 0, "MxArgs is copied in 16-byte words");
+    const int4* src = reinterpret_cast<const int4*>(&pa);
+    int4* dst = reinterpret_cast<int4*>(&p);
+    for (int i = tid; i < (int)(sizeof(MxArgs) / 16); i += kThreads) dst[i] = src[i];
+    __syncthreads();
+  }
   const int S = p.stages, NR = p.nsc;
   const int K = p.K, G = K / 32, Nw = p.Nw, nb = p.nb;
   const int nkc = (K + kKC - 1) / kKC, nfull = K / kKC;
@@ -514,9 +530,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
     ptx::tmem_relinquish();
   }
   if (warp == 4 && lane == 0) {
-    ptx::tma_prefetch_desc(&p.tm_a);
-    ptx::tma_prefetch_desc(&p.tm_b);
-    if (p.b_mode != kBStage && nfull > 0) ptx::tma_prefetch_desc(&p.tm_b3);
+    ptx::tma_prefetch_desc(&pa.tm_a);
+    ptx::tma_prefetch_desc(&pa.tm_b);
+    if (p.b_mode != kBStage && nfull > 0) ptx::tma_prefetch_desc(&pa.tm_b3);
   }
   pdl_wait();  // the logits / routing and the B operands come from the previous kernels
   pdl_launch();
@@ -553,8 +569,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
         // every token's B tiles and scale rows, once
         const uint32_t rb = ptx::smem_addr(res);
         ptx::mbar_arrive_expect_tx(resb, (uint32_t)(nkc * nb * 128 + kTerms * p.T * p.gp));
-        if (nfull > 0) ptx::tma_load_3d(rb, &p.tm_b3, resb, 0, 0, 0);
-        if (nfull < nkc) ptx::tma_load_2d(rb + nfull * nb * 128, &p.tm_b, resb, nfull * 128, 0);
+        if (nfull > 0) ptx::tma_load_3d(rb, &pa.tm_b3, resb, 0, 0, 0);
+        if (nfull < nkc) ptx::tma_load_2d(rb + nfull * nb * 128, &pa.tm_b, resb, nfull * 128, 0);
         ptx::bulk_load(rb + L.res_b, p.bsf, (uint32_t)(kTerms * p.T * p.gp), resb);
       }
       for (int it = 0; it < n_my && ok; ++it) {
@@ -580,8 +596,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
           ptx::bulk_load(scb, p.bsf + (int64_t)b0 * p.gp, (uint32_t)(nbv * p.gp), itemb(b));
         }
         if (p.b_mode == kBItem) {
-          if (nfull > 0) ptx::tma_load_3d(sbt, &p.tm_b3, itemb(b), 0, b0, 0);
-          if (nfull < nkc) ptx::tma_load_2d(sbt + nfull * nb * 128, &p.tm_b, itemb(b), nfull * 128, b0);
+          if (nfull > 0) ptx::tma_load_3d(sbt, &pa.tm_b3, itemb(b), 0, b0, 0);
+          if (nfull < nkc) ptx::tma_load_2d(sbt + nfull * nb * 128, &pa.tm_b, itemb(b), nfull * 128, b0);
         }
         ++n_issued;
         for (int kc = 0; kc < nkc; ++kc, ++g) {
@@ -592,12 +608,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
           }
           const uint32_t sa = smem0 + s * L.stage;
           ptx::mbar_arrive_expect_tx(data(s), (uint32_t)(gather ? kBM * 128 + nbv * 128 : L.stage));
-          ptx::tma_load_2d(sa, &p.tm_a, data(s), kc * 128, e * Nw + r0);
-          if (p.b_mode == kBStage) ptx::tma_load_2d(sa + kBM * 128, &p.tm_b, data(s), kc * 128, b0);
+          ptx::tma_load_2d(sa, &pa.tm_a, data(s), kc * 128, e * Nw + r0);
+          if (p.b_mode == kBStage) ptx::tma_load_2d(sa + kBM * 128, &pa.tm_b, data(s), kc * 128, b0);
           if (gather) {
             // one 4-row box per token of the group (the stage's count covers exactly these)
             for (int j = 0; j < (gr.x >> 16); ++j)
-              ptx::tma_load_2d(sa + kBM * 128 + j * kTerms * 128, &p.tm_b, data(s), kc * 128,
+              ptx::tma_load_2d(sa + kBM * 128 + j * kTerms * 128, &pa.tm_b, data(s), kc * 128,
                                (s_slot[gr.y + j] / p.k) * kTerms);
           }
         }
@@ -795,8 +811,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
             r[jj] = swiglu(gate, up, p.alpha, p.limit);
           }
           const int i = (r0 + lrow) >> 1, I = Nw >> 1;
-#pragma unroll
-          for (int term = 0; term < kTerms; ++term) {
+          // a single pass (few tokens: its latency is exposed) loops over the
+          // terms; items with more tokens (throughput) run them unrolled
+          auto term_step = [&](int term) {
 #pragma unroll
             for (int jj = 0; jj < 4; ++jj) {
               const float m = group_max<32>(fabsf(r[jj]));
@@ -817,6 +834,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
                 if (lane == 0 && !(warp & 1)) p.hs[hr * p.gp_out + (i >> 5)] = (uint8_t)sb;
               }
             }
+          };
+          if (nchunk == 1) {
+#pragma unroll 1
+            for (int term = 0; term < kTerms; ++term) term_step(term);
+          } else {
+#pragma unroll
+            for (int term = 0; term < kTerms; ++term) term_step(term);
           }
         }
       }
