@@ -561,26 +561,34 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
   auto nbrows = [&](int2 gr) { return (MODE == 0 && !gather) ? kTerms * p.T : kTerms * (gr.x >> 16); };
 
   if (warp == 4) {
-    // ---------------------------------------------------------- TMA producer (one thread)
-    if (lane == 0) {
-      int g = 0, n_issued = 0;
-      bool ok = true;
-      if (p.b_mode == kBResident && n_my > 0) {
-        // every token's B tiles and scale rows, once
-        const uint32_t rb = ptx::smem_addr(res);
-        ptx::mbar_arrive_expect_tx(resb, (uint32_t)(nkc * nb * 128 + kTerms * p.T * p.gp));
-        if (nfull > 0) ptx::tma_load_3d(rb, &pa.tm_b3, resb, 0, 0, 0);
-        if (nfull < nkc) ptx::tma_load_2d(rb + nfull * nb * 128, &pa.tm_b, resb, nfull * 128, 0);
-        ptx::bulk_load(rb + L.res_b, p.bsf, (uint32_t)(kTerms * p.T * p.gp), resb);
-      }
-      for (int it = 0; it < n_my && ok; ++it) {
-        const int item = item_of(it);
-        const int2 gr = s_grp[item / per_e];
-        const int e = gr.x & 0xFFFF, r0 = (item % per_e) * kBM;
-        const int nrows = min(kBM, Nw - r0), nbv = nbrows(gr), b0 = brow0(gr);
-        const int b = it % NR;
-        if (it >= NR && !ptx::mbar_wait(bfree(b), ((it / NR) - 1) & 1, &abort_flag)) break;
-        const uint32_t sbt = ptx::smem_addr(ring0 + b * L.ring), sca = sbt + L.ring_b, scb = sca + L.ring_sa;
+    // ---------------------------------------------------------- TMA producer (one warp)
+    // Lane 0 waits and issues the weight tiles; with gathered B, lane j
+    // issues token j's boxes (one thread issuing 17 copies a stage was the
+    // limit at 64 tokens).
+    const uint32_t full = 0xffffffffu;
+    int g = 0, n_issued = 0;
+    bool ok = true;
+    if (lane == 0 && p.b_mode == kBResident && n_my > 0) {
+      // every token's B tiles and scale rows, once
+      const uint32_t rb = ptx::smem_addr(res);
+      ptx::mbar_arrive_expect_tx(resb, (uint32_t)(nkc * nb * 128 + kTerms * p.T * p.gp));
+      if (nfull > 0) ptx::tma_load_3d(rb, &pa.tm_b3, resb, 0, 0, 0);
+      if (nfull < nkc) ptx::tma_load_2d(rb + nfull * nb * 128, &pa.tm_b, resb, nfull * 128, 0);
+      ptx::bulk_load(rb + L.res_b, p.bsf, (uint32_t)(kTerms * p.T * p.gp), resb);
+    }
+    for (int it = 0; it < n_my && ok; ++it) {
+      const int item = item_of(it);
+      const int2 gr = s_grp[item / per_e];
+      const int e = gr.x & 0xFFFF, r0 = (item % per_e) * kBM, ntok = gr.x >> 16;
+      const int nrows = min(kBM, Nw - r0), nbv = nbrows(gr), b0 = brow0(gr);
+      const int b = it % NR;
+      bool w = true;
+      if (lane == 0 && it >= NR) w = ptx::mbar_wait(bfree(b), ((it / NR) - 1) & 1, &abort_flag);
+      if (!__shfl_sync(full, w, 0)) break;
+      const uint32_t sbt = ptx::smem_addr(ring0 + b * L.ring), sca = sbt + L.ring_b, scb = sca + L.ring_sa;
+      // gathered B: this lane's token (its first term row)
+      const int trow = (gather && lane < ntok) ? (s_slot[gr.y + lane] / p.k) * kTerms : 0;
+      if (lane == 0) {
         // the item's scale rows (A contiguous [rows][G], B [nbv][gp]) and, per
         // item, its B tiles for all of K
         uint32_t tx = nrows * G;
@@ -588,46 +596,46 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
         if (p.b_mode == kBItem) tx += nkc * nb * 128;
         ptx::mbar_arrive_expect_tx(itemb(b), tx);
         ptx::bulk_load(sca, p.scales + ((int64_t)e * Nw + r0) * G, (uint32_t)(nrows * G), itemb(b));
-        if (gather) {
-          for (int j = 0; j < (gr.x >> 16); ++j)
-            ptx::bulk_load(scb + j * kTerms * p.gp, p.bsf + (int64_t)(s_slot[gr.y + j] / p.k) * kTerms * p.gp,
-                           (uint32_t)(kTerms * p.gp), itemb(b));
-        } else if (p.b_mode != kBResident) {
+        if (!gather && p.b_mode != kBResident)
           ptx::bulk_load(scb, p.bsf + (int64_t)b0 * p.gp, (uint32_t)(nbv * p.gp), itemb(b));
-        }
         if (p.b_mode == kBItem) {
           if (nfull > 0) ptx::tma_load_3d(sbt, &pa.tm_b3, itemb(b), 0, b0, 0);
           if (nfull < nkc) ptx::tma_load_2d(sbt + nfull * nb * 128, &pa.tm_b, itemb(b), nfull * 128, b0);
         }
-        ++n_issued;
-        for (int kc = 0; kc < nkc; ++kc, ++g) {
-          const int s = g % S;
-          if (g >= S && !ptx::mbar_wait(empty(s), ((g / S) - 1) & 1, &abort_flag)) {
-            ok = false;
-            break;
-          }
-          const uint32_t sa = smem0 + s * L.stage;
+      }
+      __syncwarp();
+      if (gather && lane < ntok)
+        ptx::bulk_load(scb + lane * kTerms * p.gp, p.bsf + (int64_t)trow * p.gp, (uint32_t)(kTerms * p.gp),
+                       itemb(b));
+      ++n_issued;
+      for (int kc = 0; kc < nkc; ++kc, ++g) {
+        const int s = g % S;
+        if (lane == 0 && g >= S) w = ptx::mbar_wait(empty(s), ((g / S) - 1) & 1, &abort_flag);
+        if (!__shfl_sync(full, w, 0)) {
+          ok = false;
+          break;
+        }
+        const uint32_t sa = smem0 + s * L.stage;
+        if (lane == 0) {
           ptx::mbar_arrive_expect_tx(data(s), (uint32_t)(gather ? kBM * 128 + nbv * 128 : L.stage));
           ptx::tma_load_2d(sa, &pa.tm_a, data(s), kc * 128, e * Nw + r0);
           if (p.b_mode == kBStage) ptx::tma_load_2d(sa + kBM * 128, &pa.tm_b, data(s), kc * 128, b0);
-          if (gather) {
-            // one 4-row box per token of the group (the stage's count covers exactly these)
-            for (int j = 0; j < (gr.x >> 16); ++j)
-              ptx::tma_load_2d(sa + kBM * 128 + j * kTerms * 128, &pa.tm_b, data(s), kc * 128,
-                               (s_slot[gr.y + j] / p.k) * kTerms);
-          }
         }
+        __syncwarp();
+        // one 4-row box per token of the group (the stage's count covers exactly these)
+        if (gather && lane < ntok)
+          ptx::tma_load_2d(sa + kBM * 128 + lane * kTerms * 128, &pa.tm_b, data(s), kc * 128, trow);
       }
-      if (abort_flag) {
-        // after a timeout elsewhere: let this CTA's copies in flight land
-        // (bounded) before it exits
-        volatile int quiet = 0;
-        for (int gg = max(0, g - S); gg < g; ++gg)
-          ptx::mbar_wait(data(gg % S), (gg / S) & 1, &quiet, 100000000LL);
-        for (int i2 = max(0, n_issued - NR); i2 < n_issued; ++i2)
-          ptx::mbar_wait(itemb(i2 % NR), (i2 / NR) & 1, &quiet, 100000000LL);
-        if (p.b_mode == kBResident && n_my > 0) ptx::mbar_wait(resb, 0, &quiet, 100000000LL);
-      }
+    }
+    if (lane == 0 && abort_flag) {
+      // after a timeout elsewhere: let this CTA's copies in flight land
+      // (bounded) before it exits
+      volatile int quiet = 0;
+      for (int gg = max(0, g - S); gg < g; ++gg)
+        ptx::mbar_wait(data(gg % S), (gg / S) & 1, &quiet, 100000000LL);
+      for (int i2 = max(0, n_issued - NR); i2 < n_issued; ++i2)
+        ptx::mbar_wait(itemb(i2 % NR), (i2 / NR) & 1, &quiet, 100000000LL);
+      if (p.b_mode == kBResident && n_my > 0) ptx::mbar_wait(resb, 0, &quiet, 100000000LL);
     }
     __syncwarp();
   } else if (warp == 5) {
