@@ -453,7 +453,7 @@ def run_bench_ep(args, rank, world, local, shape, case_id, T_total):
     """The same layer split over `world` ranks: experts [r*E/R, (r+1)*E/R) and
     T/R tokens per rank (strong scaling: the 8192-token batch is fixed)."""
     import torch.distributed as dist
-    from blockstreamer_b200.expert_parallel import ExpertParallelMoE, shard_experts
+    from blockstreamer_b200.expert_parallel import ExpertParallelMoE, P2PExchange, shard_experts
 
     dev = torch.device("cuda", local)
     if T_total % world:
@@ -468,7 +468,10 @@ def run_bench_ep(args, rank, world, local, shape, case_id, T_total):
     x = x_all[rank * Tr:(rank + 1) * Tr].contiguous()
     del x_all
     torch.cuda.empty_cache()
-    layer = ExpertParallelMoE(shape.experts, shape.top_k)
+    exchange = None
+    if args.ep_transport == "p2p":
+        exchange = P2PExchange(None, shape.experts, shape.hidden, Tr, shape.top_k, dev)
+    layer = ExpertParallelMoE(shape.experts, shape.top_k, exchange=exchange)
 
     def step():
         return layer(x, router_w, router_b, local_p)
@@ -517,7 +520,15 @@ def run_bench_ep(args, rank, world, local, shape, case_id, T_total):
     e2e_ms = max_over_ranks(statistics.mean(e2e), world)
     stats = layer.last_stats
     peaks, peak_src = load_peaks()
-    S_local = sum(stats.rows_received)
+    if exchange is not None:
+        S_local = int(exchange.local_offsets[-1].item())
+        sent = received = None
+        collective = ("peer-memory exchange over NVLink (bs_ep_p2p_*: counts, rows and results stored "
+                      "into the peers' buffers by the library's kernels, epoch flags, no host sync)")
+    else:
+        S_local = sum(stats.rows_received)
+        sent, received = stats.rows_sent, stats.rows_received
+        collective = "NCCL all_to_all_single (counts, dispatch rows, combine rows)"
     exp_ms = stage_ms.get("experts", 0.0)
     exp_flops = S_local * 6.0 * shape.hidden * shape.intermediate
     achieved = exp_flops / (exp_ms * 1e-3) / 1e12 if exp_ms else 0.0
@@ -528,10 +539,10 @@ def run_bench_ep(args, rank, world, local, shape, case_id, T_total):
                 "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
                 "config": {"workload": args.workload, "tokens": T_total, "tokens_per_rank": Tr,
                            "experts_per_rank": shape.experts // world, "parallelism": f"ep{world}",
-                           "collective": "NCCL all_to_all_single (counts, dispatch rows, combine rows)",
+                           "collective": collective,
                            "l2": "inputs larger than L2 (expert weights + dispatched rows per rank)",
-                           "rank0_rows_sent": stats.rows_sent,
-                           "rank0_rows_received": stats.rows_received},
+                           "rank0_rows_sent": sent, "rank0_rows_received": received,
+                           "rank0_rows_processed": S_local},
                 "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                              "frac": achieved / peak if peak else None, "traffic": None,
                              "kernel": "experts (gate_up + down, rank 0)",
@@ -541,8 +552,10 @@ def run_bench_ep(args, rank, world, local, shape, case_id, T_total):
                         "h2d_bytes_per_step": x.numel() * 2 * world,
                         "d2h_bytes_per_step": x.numel() * 2 * world,
                         "api": "blockstreamer_b200.expert_parallel.ExpertParallelMoE"},
-                "clocks": clk.summary(), "gpu_launches": 14 * args.steps}
+                "clocks": clk.summary(), "gpu_launches": (14 if exchange is not None else 12) * args.steps}
         print(json.dumps(line), flush=True)
+    if exchange is not None:
+        exchange.close()
 
 
 def main():
@@ -555,6 +568,8 @@ def main():
     ap.add_argument("--algo", choices=["auto", "gemv", "tcgen05", "mx"], default="auto")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-graph", action="store_true", help="decode shapes: launch eagerly")
+    ap.add_argument("--ep-transport", choices=["p2p", "nccl"], default="p2p",
+                    help="N > 1: exchange rows over peer memory (library kernels) or NCCL all-to-all")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -20,16 +20,25 @@ experts) and its own share of the tokens.  One forward:
 The exchange is the only collective; each rank's kernels are the single-GPU
 ones.  ``ops`` abstracts the per-rank compute so that the orchestration can be
 checked with CPU ranks (gloo) against a single-process evaluation.
+
+On GPUs the exchange can instead run over peer memory (``P2PExchange``,
+``bs_ep_p2p_*``): each rank's rows are stored straight into the destination
+rank's buffer in the expert-major order its grouped GEMMs read, and each
+result straight back into its source's buffer in dispatch order, by the
+library's own kernels with epoch flags -- no host synchronization (NCCL's
+uneven all-to-all needs the split sizes on the host), no regroup or ungroup
+pass, no library collective on the data path.
 """
 
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import torch
 import torch.distributed as dist
 
-from . import kernels
+from . import _lib, kernels
 
 
 class CudaOps:
@@ -74,6 +83,89 @@ def shard_experts(params: dict, rank: int, world: int) -> dict:
     return out
 
 
+class _DeviceBytes:
+    """A raw device allocation seen by torch (zero-copy, __cuda_array_interface__)."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class P2PExchange:
+    """One rank's peer-memory exchange buffer and its peers' mappings.
+
+    Collective over ``group``: every rank constructs it with the same
+    arguments.  ``max_tokens`` bounds the tokens a rank dispatches per call;
+    the receive area holds every rank's rows (R * max_tokens * top_k), so no
+    routing can overflow it."""
+
+    def __init__(self, group, num_experts: int, hidden: int, max_tokens: int, top_k: int, device):
+        self.group = group
+        self.R = dist.get_world_size(group)
+        self.me = dist.get_rank(group)
+        self.E, self.H, self.k = num_experts, hidden, top_k
+        self.src_rows = max_tokens * top_k
+        self.cap = self.R * self.src_rows
+        self.device = torch.device(device)
+        lib = _lib.load()
+        nbytes = lib.bs_ep_p2p_bytes(self.R, self.E, self.H, self.cap, self.src_rows)
+        base, handle = ctypes.c_void_p(), (ctypes.c_char * 64)()
+        with torch.cuda.device(self.device):
+            _lib.call("bs_ep_p2p_alloc", nbytes, ctypes.byref(base), handle)
+        self.base = base.value
+        handles = [None] * self.R
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.peers = []
+        with torch.cuda.device(self.device):
+            for s, hs in enumerate(handles):
+                if s == self.me:
+                    self.peers.append(self.base)
+                    continue
+                pb = ctypes.c_void_p()
+                _lib.call("bs_ep_p2p_open", ctypes.create_string_buffer(hs, 64), ctypes.byref(pb))
+                self.peers.append(pb.value)
+        self.bases = torch.tensor(self.peers, dtype=torch.int64, device=self.device)
+        ro, yo = ctypes.c_size_t(), ctypes.c_size_t()
+        _lib.call("bs_ep_p2p_layout", self.R, self.E, self.H, self.cap, self.src_rows, ctypes.byref(ro),
+                  ctypes.byref(yo))
+        raw = torch.as_tensor(_DeviceBytes(self.base, nbytes), device=self.device)
+        self.recv = raw[ro.value: ro.value + self.cap * self.H * 2].view(torch.bfloat16).view(self.cap, self.H)
+        self.yback = raw[yo.value: yo.value + self.src_rows * self.H * 2].view(torch.bfloat16).view(
+            self.src_rows, self.H)
+        self.local_offsets = torch.zeros(self.E // self.R + 1, dtype=torch.int32, device=self.device)
+        self.epoch = 0
+        self._closed = False
+
+    def dispatch(self, x: torch.Tensor, expert_offsets: torch.Tensor, token_of_row: torch.Tensor):
+        self.epoch = (self.epoch + 1) & 0xFFFFFFFF
+        with torch.cuda.device(self.device):
+            _lib.call("bs_ep_p2p_dispatch", x.data_ptr(), self.H, expert_offsets.data_ptr(),
+                      token_of_row.data_ptr(), self.base, self.bases.data_ptr(), self.R, self.E, self.me,
+                      self.cap, self.src_rows, self.epoch, self.local_offsets.data_ptr(),
+                      torch.cuda.current_stream(self.device).cuda_stream)
+
+    def give_back(self, y: torch.Tensor):
+        with torch.cuda.device(self.device):
+            _lib.call("bs_ep_p2p_return", y.data_ptr(), self.H, self.base, self.bases.data_ptr(), self.R,
+                      self.E, self.me, self.cap, self.src_rows, self.epoch,
+                      torch.cuda.current_stream(self.device).cuda_stream)
+
+    def close(self):
+        """Collective: unmap the peers, then free this rank's buffer."""
+        if self._closed:
+            return
+        self._closed = True
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            for s, pb in enumerate(self.peers):
+                if s != self.me:
+                    _lib.call("bs_ep_p2p_close", pb)
+        dist.barrier(group=self.group)
+        with torch.cuda.device(self.device):
+            _lib.call("bs_ep_p2p_free", self.base)
+
+
 @dataclass
 class EPStats:
     rows_sent: list
@@ -84,7 +176,8 @@ class ExpertParallelMoE:
     """One gpt-oss MoE layer sharded by expert over a process group."""
 
     def __init__(self, num_experts: int, top_k: int, group=None, ops=None,
-                 alpha: float = kernels.ALPHA, limit: float = kernels.LIMIT):
+                 alpha: float = kernels.ALPHA, limit: float = kernels.LIMIT,
+                 exchange: P2PExchange | None = None):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -96,6 +189,9 @@ class ExpertParallelMoE:
         self.ops = ops if ops is not None else CudaOps()
         self.alpha, self.limit = alpha, limit
         self.last_stats: EPStats | None = None
+        # peer-memory exchange (GPUs); None: NCCL / gloo all-to-all
+        self.exchange = exchange
+        self._h = self._y = None
         # optional: a list that receives (stage name, CUDA event) at stage ends
         self.marks: list | None = None
 
@@ -110,6 +206,8 @@ class ExpertParallelMoE:
         """x: this rank's tokens [T_r, H].  ``local_experts`` holds this rank's
         slice of the six expert tensors (names without the ``experts.`` prefix).
         Returns (out [T_r, H], scores [T_r, k], indices [T_r, k] global)."""
+        if self.exchange is not None:
+            return self._forward_p2p(x, router_weight, router_bias, local_experts)
         R, El, k = self.world, self.El, self.top_k
         T, H = x.shape
         ops = self.ops
@@ -142,6 +240,34 @@ class ExpertParallelMoE:
         out = ops.combine(y_back, row_of_slot, sc, T)
         self._mark("combine")
         self.last_stats = EPStats(send_rows, recv_rows)
+        return out, sc, idx
+
+    def _forward_p2p(self, x, router_weight, router_bias, p):
+        ex, k = self.exchange, self.top_k
+        T, H = x.shape
+        if T * k > ex.src_rows:
+            raise ValueError(f"{T} tokens exceed the exchange's {ex.src_rows // k} per rank")
+        self._mark("start")
+        sc, idx = self.ops.router(x, router_weight, router_bias, k)
+        self._mark("router")
+        d = kernels.dispatch(idx, self.E)
+        self._mark("dispatch")
+        ex.dispatch(x, d.expert_offsets, d.token_of_row)
+        self._mark("exchange_dispatch")
+        if self._h is None:
+            I = p["gate_up_proj_blocks"].shape[1] // 2
+            self._h = torch.empty(ex.cap, I, dtype=torch.bfloat16, device=x.device)
+            self._y = torch.empty(ex.cap, H, dtype=torch.bfloat16, device=x.device)
+        algo = getattr(self.ops, "algo", kernels.ALGO_AUTO)
+        kernels.moe_gate_up(ex.recv, ex.local_offsets, p["gate_up_proj_blocks"], p["gate_up_proj_scales"],
+                            p["gate_up_proj_bias"], alpha=self.alpha, limit=self.limit, algo=algo, out=self._h)
+        kernels.moe_down(self._h, ex.local_offsets, p["down_proj_blocks"], p["down_proj_scales"],
+                         p["down_proj_bias"], algo=algo, out=self._y)
+        self._mark("experts")
+        ex.give_back(self._y)
+        self._mark("exchange_combine")
+        out = kernels.combine(ex.yback[: T * k], d.row_of_slot, sc, T)
+        self._mark("combine")
         return out, sc, idx
 
     __call__ = forward

@@ -166,6 +166,50 @@ int bs_ep_regroup(const int32_t* recv_counts, int64_t R, int64_t El, const void*
 int bs_gather_rows(const void* src, const int32_t* row_map, int64_t rows, int64_t H, void* dst,
                    void* stream);
 
+/* Expert-parallel exchange over peer memory (NVLink), the B200 form of the
+ * all-to-all steps around block_streamer/gptoss.py:149-176 when the experts are
+ * sharded over R GPUs (the reference has no distributed backend): no host
+ * synchronization, no library collective, plain peer stores (no multicast).
+ * Set-up, once per rank (collective over the ranks by the caller):
+ *   bs_ep_p2p_bytes(R, E, H, cap_rows, src_rows) -> bytes of the rank's
+ *     exchange buffer; src_rows = max dispatched rows per rank (tokens * k),
+ *     cap_rows >= R * src_rows rows this rank's experts may receive;
+ *   bs_ep_p2p_alloc(bytes, &base, handle[64]) allocates it (cudaMalloc,
+ *     zeroed) and returns its CUDA IPC handle; exchange the handles between
+ *     the ranks; bs_ep_p2p_open(peer handle, &peer_base) maps a peer's buffer;
+ *   the caller places the R bases (its own at index me) in a device array.
+ *   bs_ep_p2p_close / bs_ep_p2p_free undo them (free after every peer closed).
+ * bs_ep_p2p_layout gives the byte offsets of recv [cap_rows, H] bf16 (the rows
+ * this rank's experts process, expert-major, then by source rank) and yback
+ * [src_rows, H] bf16 (this rank's dispatched rows' expert results, in its
+ * dispatch order) inside a buffer.
+ * Per layer call, with an epoch that increases by one per call on every rank:
+ *   bs_ep_p2p_dispatch: from this rank's dispatch (bs_dispatch with x NULL:
+ *     expert_offsets [E+1] over GLOBAL experts, token_of_row) and its tokens
+ *     x [T, H] bf16, sends every row to its expert's rank; when it returns on
+ *     the stream, recv holds every source's rows and local_offsets [E/R + 1]
+ *     their expert offsets;
+ *   (run gate_up + down on recv with local_offsets, results [cap_rows, H])
+ *   bs_ep_p2p_return: sends each result row back to its source's yback; when
+ *     it returns on the stream, this rank's yback is complete (combine it with
+ *     row_of_slot).
+ * Every wait for a peer is bounded (~2 s); a timeout is reported through
+ * bs_device_status as BS_ERR_TIMEOUT. */
+size_t bs_ep_p2p_bytes(int64_t R, int64_t E, int64_t H, int64_t cap_rows, int64_t src_rows);
+int bs_ep_p2p_layout(int64_t R, int64_t E, int64_t H, int64_t cap_rows, int64_t src_rows,
+                     size_t* recv_offset, size_t* yback_offset);
+int bs_ep_p2p_alloc(size_t bytes, void** base, void* ipc_handle);
+int bs_ep_p2p_open(const void* ipc_handle, void** peer_base);
+int bs_ep_p2p_close(void* peer_base);
+int bs_ep_p2p_free(void* base);
+int bs_ep_p2p_dispatch(const void* x, int64_t H, const int32_t* expert_offsets,
+                       const int32_t* token_of_row, void* my_base, const uint64_t* peer_bases,
+                       int64_t R, int64_t E, int64_t me, int64_t cap_rows, int64_t src_rows,
+                       uint32_t epoch, int32_t* local_offsets, void* stream);
+int bs_ep_p2p_return(const void* y, int64_t H, void* my_base, const uint64_t* peer_bases,
+                     int64_t R, int64_t E, int64_t me, int64_t cap_rows, int64_t src_rows,
+                     uint32_t epoch, void* stream);
+
 /* One expert projection without activation: out[m, N] = x[m, K] @ dequant(W) (+ bias).
  * Replaces block_streamer/gptoss.py:74-75 (mxfp4_matmul forward) for one expert:
  * blocks [N, K/32, 16], scales [N, K/32], x [m, K] bf16, out [m, N] bf16;

@@ -1,0 +1,83 @@
+"""One rank of the multi-GPU expert-parallel parity check (run by torchrun
+from tests/test_gpu_ep.py; not collected by pytest).
+
+Each rank owns E/R experts and T/R tokens.  For each case the layer output of
+the rank's tokens is compared with the single-GPU layer on all tokens (the
+same library kernels, so routing and results must agree), once through the
+peer-memory exchange and once through NCCL all-to-all, over three successive
+calls (the peer-memory flags and buffers are reused across calls); the two
+exchanges must give bit-identical outputs.  Exits non-zero on any mismatch."""
+
+import datetime
+import os
+import sys
+
+import torch
+import torch.distributed as dist
+
+REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, REPO)
+
+from blockstreamer_b200 import kernels  # noqa: E402
+from blockstreamer_b200.expert_parallel import CudaOps, ExpertParallelMoE, P2PExchange, shard_experts  # noqa: E402
+from blockstreamer_b200.synthetic import CASES, LayerShape, make_layer, make_tokens  # noqa: E402
+
+
+def rel_l2(a, b):
+    a, b = a.float(), b.float()
+    return float((a - b).norm() / b.norm().clamp_min(1e-30))
+
+
+def main():
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=60), device_id=dev)
+    cases = [("small", LayerShape(512, 512, 16, 4), 7, 64 * world),
+             ("gptoss120b", CASES["gptoss120b"], 4, 256 * world)]
+    algo = kernels.ALGO_TCGEN05
+    ok = True
+    for name, shape, case_id, T in cases:
+        full = make_layer(shape, case_id, device=dev)
+        x_all = make_tokens(T, shape.hidden, case_id, device=dev)
+        pe = {k.split(".", 1)[1]: v for k, v in full.items() if k.startswith("experts.")}
+        ref, _, idx_ref = kernels.moe_forward(
+            x_all, pe["gate_up_proj_blocks"], pe["gate_up_proj_scales"], pe["gate_up_proj_bias"],
+            pe["down_proj_blocks"], pe["down_proj_scales"], pe["down_proj_bias"], shape.top_k,
+            router_weight=full["router.weight"], router_bias=full["router.bias"], algo=algo)
+        Tr = T // world
+        sl = slice(rank * Tr, (rank + 1) * Tr)
+        x = x_all[sl].contiguous()
+        local_p = shard_experts(pe, rank, world)
+        outs = {}
+        for transport in ("p2p", "nccl"):
+            ex = P2PExchange(None, shape.experts, shape.hidden, Tr, shape.top_k, dev) if transport == "p2p" else None
+            layer = ExpertParallelMoE(shape.experts, shape.top_k, ops=CudaOps(algo), exchange=ex)
+            for call in range(3):
+                out, _, idx = layer(x, full["router.weight"], full["router.bias"], local_p)
+                torch.cuda.synchronize()
+                same = (idx.long() == idx_ref[sl].long()).all(1)
+                rel = rel_l2(out[same], ref[sl][same])
+                good = bool(same.float().mean() >= 0.99) and rel <= 1e-3
+                print(f"rank {rank} {name} {transport} call {call}: routing match {same.float().mean():.4f} "
+                      f"rel_l2 vs single GPU {rel:.2e} {'ok' if good else 'MISMATCH'}", flush=True)
+                ok &= good
+            outs[transport] = out.clone()
+            status = kernels.device_status(clear=True)
+            if status:
+                print(f"rank {rank} {name} {transport}: device status {status}", flush=True)
+                ok = False
+            if ex is not None:
+                ex.close()
+        same_bits = torch.equal(outs["p2p"], outs["nccl"])
+        print(f"rank {rank} {name}: p2p and nccl outputs bit-identical: {same_bits}", flush=True)
+        ok &= same_bits
+    flag = torch.tensor([0 if ok else 1], device=dev)
+    dist.all_reduce(flag)
+    dist.destroy_process_group()
+    sys.exit(1 if int(flag.item()) else 0)
+
+
+if __name__ == "__main__":
+    main()
