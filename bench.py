@@ -479,6 +479,19 @@ def run_bench_ep(args, rank, world, local, shape, case_id, T_total):
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
+    # The peer-memory path has no host synchronization: one layer call is
+    # captured as a CUDA graph (per rank) and replayed; x is its static input.
+    graph = None
+    if exchange is not None and not args.no_graph:
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            g_out = step()
+        torch.cuda.synchronize()
+    eager_step = step
+    if graph is not None:
+        def step():
+            graph.replay()
+            return g_out
     st = torch.cuda.current_stream()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
@@ -492,11 +505,11 @@ def run_bench_ep(args, rank, world, local, shape, case_id, T_total):
         barrier(world)
     ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world)
     value = T_total / (ms * 1e-3)
-    # per-stage breakdown (same steps, events at stage boundaries)
+    # per-stage breakdown (same steps launched eagerly, events at stage boundaries)
     stage_ms = {}
     for _ in range(args.steps):
         layer.marks = []
-        step()
+        eager_step()
         torch.cuda.synchronize()
         for (_, a), (name, b) in zip(layer.marks[:-1], layer.marks[1:]):
             stage_ms[name] = stage_ms.get(name, 0.0) + a.elapsed_time(b) / args.steps
@@ -504,14 +517,14 @@ def run_bench_ep(args, rank, world, local, shape, case_id, T_total):
     # e2e: this rank's tokens in from pinned host memory, its output back out
     x_host = x.cpu().pin_memory()
     out_host = torch.empty_like(x_host).pin_memory()
-    x_dev = torch.empty_like(x)
+    x_dev = x if graph is not None else torch.empty_like(x)   # the graph's input buffer
     e2e = []
     for i in range(args.warmup + args.steps):
         barrier(world)
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(st)
         x_dev.copy_(x_host, non_blocking=True)
-        o, _, _ = layer(x_dev, router_w, router_b, local_p)
+        o, _, _ = step() if graph is not None else layer(x_dev, router_w, router_b, local_p)
         out_host.copy_(o, non_blocking=True)
         b.record(st)
         b.synchronize()
@@ -542,7 +555,7 @@ def run_bench_ep(args, rank, world, local, shape, case_id, T_total):
                            "collective": collective,
                            "l2": "inputs larger than L2 (expert weights + dispatched rows per rank)",
                            "rank0_rows_sent": sent, "rank0_rows_received": received,
-                           "rank0_rows_processed": S_local},
+                           "rank0_rows_processed": S_local, "cuda_graph": graph is not None},
                 "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                              "frac": achieved / peak if peak else None, "traffic": None,
                              "kernel": "experts (gate_up + down, rank 0)",
@@ -554,6 +567,7 @@ def run_bench_ep(args, rank, world, local, shape, case_id, T_total):
                         "api": "blockstreamer_b200.expert_parallel.ExpertParallelMoE"},
                 "clocks": clk.summary(), "gpu_launches": (14 if exchange is not None else 12) * args.steps}
         print(json.dumps(line), flush=True)
+    del graph
     if exchange is not None:
         exchange.close()
 

@@ -51,9 +51,8 @@ SIGNATURES = {
     "bs_ep_p2p_open": (_i32, [_vp, _c.POINTER(_vp)]),
     "bs_ep_p2p_close": (_i32, [_vp]),
     "bs_ep_p2p_free": (_i32, [_vp]),
-    "bs_ep_p2p_dispatch": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64,
-                                  _c.c_uint32, _vp, _vp]),
-    "bs_ep_p2p_return": (_i32, [_vp, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _c.c_uint32, _vp]),
+    "bs_ep_p2p_dispatch": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp]),
+    "bs_ep_p2p_return": (_i32, [_vp, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp]),
     "bs_combine": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp]),
     "bs_mxfp4_matmul": (_i32, [_vp, _i64, _i64, _vp, _vp, _i64, _vp, _vp, _i32, _vp]),
     "bs_moe_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64]),

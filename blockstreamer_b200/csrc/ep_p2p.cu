@@ -5,8 +5,9 @@
 // other rank's address space through CUDA IPC (plain peer loads and stores;
 // no multicast object, no TMA multicast).  Its layout (ep_layout):
 //   flags   [3][kMaxRanks] u32: counts / rows / results from source s arrived
-//           (each holds the epoch of the last layer call that set it) and two
-//           local launch counters;
+//           (each holds the epoch of the last layer call that set it), two
+//           local launch counters and this rank's epoch (layer calls so far,
+//           advanced on the device, so a captured CUDA graph replays correctly);
 //   counts  [R][E] i32: row s = source s's rows per global expert;
 //   recv    [cap_rows][H] bf16: rows this rank's experts process, expert-major
 //           and, within an expert, source-major (the grouped GEMMs read them
@@ -14,9 +15,9 @@
 //   yback   [src_rows][H] bf16: this rank's own dispatched rows' results,
 //           in its dispatch order (the combine reads them in place).
 // One layer call with epoch n (the same on every rank, increasing):
-//   1. ep_counts_kernel   publish this rank's per-expert row counts into every
-//                         rank's counts row `me`, then raise flags.counts[me]
-//                         there (release, system scope);
+//   1. ep_counts_kernel   advance the epoch; publish this rank's per-expert
+//                         row counts into every rank's counts row `me`, then
+//                         raise flags.counts[me] there (release, system scope);
 //   2. ep_scatter_kernel  wait for every source's counts (bounded), compute
 //                         where each of this rank's rows lands in its
 //                         destination's recv (expert-major), copy x[token] there
@@ -46,7 +47,7 @@ constexpr int kMaxRanks = 64;
 constexpr int kMaxExperts = 1024;
 constexpr long long kWaitCycles = 4000000000LL;
 constexpr int kCounts = 0, kRows = 1, kResults = 2;  // flag groups
-constexpr int kCtrScatter = 3 * kMaxRanks, kCtrReturn = 3 * kMaxRanks + 1;
+constexpr int kCtrScatter = 3 * kMaxRanks, kCtrReturn = 3 * kMaxRanks + 1, kEpoch = 3 * kMaxRanks + 2;
 
 struct EPLayout {
   size_t flags, counts, recv, yback, total;
@@ -58,7 +59,7 @@ __host__ __device__ inline EPLayout ep_layout(int64_t R, int64_t E, int64_t H, i
   EPLayout L;
   size_t o = 0;
   L.flags = o;
-  o = al(o + 4 * (3 * kMaxRanks + 2));
+  o = al(o + 4 * (3 * kMaxRanks + 3));
   L.counts = o;
   o = al(o + (size_t)R * E * 4);
   L.recv = o;
@@ -111,7 +112,13 @@ __device__ __forceinline__ int last_le(const int* a, int n, int v) {
 
 __global__ void __launch_bounds__(256) ep_counts_kernel(const int* __restrict__ offsets,
                                                         const uint64_t* __restrict__ bases, int R, int E,
-                                                        int me, EPLayout L, uint32_t epoch) {
+                                                        int me, EPLayout L) {
+  __shared__ uint32_t epoch;
+  if (threadIdx.x == 0) {
+    uint32_t* ep = at<uint32_t>(bases[me], L.flags) + kEpoch;
+    epoch = *ep + 1;
+    *ep = epoch;
+  }
   for (int i = threadIdx.x; i < R * E; i += blockDim.x) {
     const int d = i / E, e = i - d * E;
     at<int>(bases[d], L.counts)[me * E + e] = offsets[e + 1] - offsets[e];
@@ -126,7 +133,7 @@ __global__ void __launch_bounds__(256) ep_scatter_kernel(const uint4* __restrict
                                                          const int* __restrict__ offsets,
                                                          const int* __restrict__ token_of_row,
                                                          const uint64_t* __restrict__ bases, int R, int E,
-                                                         int me, EPLayout L, uint32_t epoch, int* status) {
+                                                         int me, EPLayout L, int* status) {
   extern __shared__ int sm[];
   int* cm = sm;            // [R][E]
   int* pos = cm + R * E;   // [E]: first recv row of this rank's rows of expert e at its destination
@@ -134,6 +141,7 @@ __global__ void __launch_bounds__(256) ep_scatter_kernel(const uint4* __restrict
   __shared__ int ok;
   const uint64_t mine = bases[me];
   uint32_t* flags = at<uint32_t>(mine, L.flags);
+  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(flags + kEpoch);
   if (threadIdx.x == 0) ok = wait_all(flags + kCounts * kMaxRanks, R, epoch, status);
   __syncthreads();
   if (!ok) return;
@@ -176,9 +184,12 @@ __global__ void __launch_bounds__(256) ep_scatter_kernel(const uint4* __restrict
 // Wait for every rank's flag of `group`; with El > 0 also write the local
 // expert offsets of recv (expert-major over the counts matrix).
 __global__ void ep_arrived_kernel(uint64_t mine, EPLayout L, int group, int R, int E, int me, int El,
-                                  int* __restrict__ local_offsets, uint32_t epoch, int* status) {
+                                  int* __restrict__ local_offsets, int* status) {
   __shared__ int ok;
-  if (threadIdx.x == 0) ok = wait_all(at<uint32_t>(mine, L.flags) + group * kMaxRanks, R, epoch, status);
+  if (threadIdx.x == 0) {
+    const uint32_t* flags = at<uint32_t>(mine, L.flags);
+    ok = wait_all(flags + group * kMaxRanks, R, *reinterpret_cast<const volatile uint32_t*>(flags + kEpoch), status);
+  }
   __syncthreads();
   if (!ok || El == 0 || threadIdx.x != 0) return;
   const volatile int* cm = at<int>(mine, L.counts);
@@ -193,7 +204,7 @@ __global__ void ep_arrived_kernel(uint64_t mine, EPLayout L, int group, int R, i
 // Dynamic shared memory: counts [R][E], loc [El + 1], seg [El][R + 1], src [El][R] (ints).
 __global__ void __launch_bounds__(256) ep_return_kernel(const uint4* __restrict__ y, int64_t vecs,
                                                         const uint64_t* __restrict__ bases, int R, int E,
-                                                        int me, EPLayout L, uint32_t epoch) {
+                                                        int me, EPLayout L) {
   extern __shared__ int sm[];
   const int El = E / R;
   int* cm = sm;                    // [R][E]
@@ -241,6 +252,7 @@ __global__ void __launch_bounds__(256) ep_return_kernel(const uint4* __restrict_
   if (threadIdx.x == 0) {
     unsigned int* ctr = reinterpret_cast<unsigned int*>(at<uint32_t>(mine, L.flags) + kCtrReturn);
     if (atomicAdd(ctr, 1u) == gridDim.x - 1) {
+      const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(at<uint32_t>(mine, L.flags) + kEpoch);
       *ctr = 0;
       __threadfence_system();
       for (int s = 0; s < R; ++s) st_release_sys(at<uint32_t>(bases[s], L.flags) + kResults * kMaxRanks + me, epoch);
@@ -317,8 +329,7 @@ int bs_ep_p2p_free(void* base) {
 
 int bs_ep_p2p_dispatch(const void* x, int64_t H, const int32_t* expert_offsets, const int32_t* token_of_row,
                        void* my_base, const uint64_t* peer_bases, int64_t R, int64_t E, int64_t me,
-                       int64_t cap_rows, int64_t src_rows, uint32_t epoch, int32_t* local_offsets,
-                       void* stream) {
+                       int64_t cap_rows, int64_t src_rows, int32_t* local_offsets, void* stream) {
   BS_TRY(check_shape(R, E, H, me));
   BS_ARG(x && expert_offsets && token_of_row && my_base && peer_bases && local_offsets,
          "bs_ep_p2p_dispatch: null pointer");
@@ -327,23 +338,23 @@ int bs_ep_p2p_dispatch(const void* x, int64_t H, const int32_t* expert_offsets, 
   const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const EPLayout L = ep_layout(R, E, H, cap_rows, src_rows);
   int* status = device_status_ptr();
-  ep_counts_kernel<<<1, 256, 0, st>>>(expert_offsets, peer_bases, (int)R, (int)E, (int)me, L, epoch);
+  ep_counts_kernel<<<1, 256, 0, st>>>(expert_offsets, peer_bases, (int)R, (int)E, (int)me, L);
   BS_CUDA(cudaGetLastError());
   const size_t smem = (size_t)(R * E + 2 * E + 1) * 4;
   BS_REQUIRE(smem <= 48 * 1024, BS_ERR_UNSUPPORTED, "bs_ep_p2p_dispatch: %lld ranks x %lld experts too large",
              (long long)R, (long long)E);
   ep_scatter_kernel<<<grid_rows(src_rows), 256, smem, st>>>(
       static_cast<const uint4*>(x), H / 8, expert_offsets, token_of_row, peer_bases, (int)R, (int)E, (int)me,
-      L, epoch, status);
+      L, status);
   BS_CUDA(cudaGetLastError());
   ep_arrived_kernel<<<1, 32, 0, st>>>(reinterpret_cast<uint64_t>(my_base), L, kRows, (int)R, (int)E, (int)me,
-                                      (int)(E / R), local_offsets, epoch, status);
+                                      (int)(E / R), local_offsets, status);
   BS_CUDA(cudaGetLastError());
   return BS_OK;
 }
 
 int bs_ep_p2p_return(const void* y, int64_t H, void* my_base, const uint64_t* peer_bases, int64_t R, int64_t E,
-                     int64_t me, int64_t cap_rows, int64_t src_rows, uint32_t epoch, void* stream) {
+                     int64_t me, int64_t cap_rows, int64_t src_rows, void* stream) {
   BS_TRY(check_shape(R, E, H, me));
   BS_ARG(y && my_base && peer_bases, "bs_ep_p2p_return: null pointer");
   BS_ALIGNED16(y, "y");
@@ -355,10 +366,10 @@ int bs_ep_p2p_return(const void* y, int64_t H, void* my_base, const uint64_t* pe
   BS_REQUIRE(smem <= 48 * 1024, BS_ERR_UNSUPPORTED, "bs_ep_p2p_return: %lld ranks x %lld experts too large",
              (long long)R, (long long)E);
   ep_return_kernel<<<grid_rows(cap_rows), 256, smem, st>>>(static_cast<const uint4*>(y), H / 8, peer_bases,
-                                                            (int)R, (int)E, (int)me, L, epoch);
+                                                            (int)R, (int)E, (int)me, L);
   BS_CUDA(cudaGetLastError());
   ep_arrived_kernel<<<1, 32, 0, st>>>(reinterpret_cast<uint64_t>(my_base), L, kResults, (int)R, (int)E, (int)me, 0,
-                                      nullptr, epoch, status);
+                                      nullptr, status);
   BS_CUDA(cudaGetLastError());
   return BS_OK;
 }

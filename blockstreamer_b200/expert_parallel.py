@@ -133,21 +133,20 @@ class P2PExchange:
         self.yback = raw[yo.value: yo.value + self.src_rows * self.H * 2].view(torch.bfloat16).view(
             self.src_rows, self.H)
         self.local_offsets = torch.zeros(self.E // self.R + 1, dtype=torch.int32, device=self.device)
-        self.epoch = 0
         self._closed = False
 
     def dispatch(self, x: torch.Tensor, expert_offsets: torch.Tensor, token_of_row: torch.Tensor):
-        self.epoch = (self.epoch + 1) & 0xFFFFFFFF
+        """Send this rank's rows (stream-ordered, no host sync; capturable in a CUDA graph)."""
         with torch.cuda.device(self.device):
             _lib.call("bs_ep_p2p_dispatch", x.data_ptr(), self.H, expert_offsets.data_ptr(),
                       token_of_row.data_ptr(), self.base, self.bases.data_ptr(), self.R, self.E, self.me,
-                      self.cap, self.src_rows, self.epoch, self.local_offsets.data_ptr(),
+                      self.cap, self.src_rows, self.local_offsets.data_ptr(),
                       torch.cuda.current_stream(self.device).cuda_stream)
 
     def give_back(self, y: torch.Tensor):
         with torch.cuda.device(self.device):
             _lib.call("bs_ep_p2p_return", y.data_ptr(), self.H, self.base, self.bases.data_ptr(), self.R,
-                      self.E, self.me, self.cap, self.src_rows, self.epoch,
+                      self.E, self.me, self.cap, self.src_rows,
                       torch.cuda.current_stream(self.device).cuda_stream)
 
     def close(self):

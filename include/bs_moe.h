@@ -183,7 +183,8 @@ int bs_gather_rows(const void* src, const int32_t* row_map, int64_t rows, int64_
  * this rank's experts process, expert-major, then by source rank) and yback
  * [src_rows, H] bf16 (this rank's dispatched rows' expert results, in its
  * dispatch order) inside a buffer.
- * Per layer call, with an epoch that increases by one per call on every rank:
+ * Per layer call (each rank counts its calls on the device, so the calls may
+ * be captured in a CUDA graph and replayed):
  *   bs_ep_p2p_dispatch: from this rank's dispatch (bs_dispatch with x NULL:
  *     expert_offsets [E+1] over GLOBAL experts, token_of_row) and its tokens
  *     x [T, H] bf16, sends every row to its expert's rank; when it returns on
@@ -205,10 +206,10 @@ int bs_ep_p2p_free(void* base);
 int bs_ep_p2p_dispatch(const void* x, int64_t H, const int32_t* expert_offsets,
                        const int32_t* token_of_row, void* my_base, const uint64_t* peer_bases,
                        int64_t R, int64_t E, int64_t me, int64_t cap_rows, int64_t src_rows,
-                       uint32_t epoch, int32_t* local_offsets, void* stream);
+                       int32_t* local_offsets, void* stream);
 int bs_ep_p2p_return(const void* y, int64_t H, void* my_base, const uint64_t* peer_bases,
                      int64_t R, int64_t E, int64_t me, int64_t cap_rows, int64_t src_rows,
-                     uint32_t epoch, void* stream);
+                     void* stream);
 
 /* One expert projection without activation: out[m, N] = x[m, K] @ dequant(W) (+ bias).
  * Replaces block_streamer/gptoss.py:74-75 (mxfp4_matmul forward) for one expert:

@@ -5,8 +5,9 @@ Each rank owns E/R experts and T/R tokens.  For each case the layer output of
 the rank's tokens is compared with the single-GPU layer on all tokens (the
 same library kernels, so routing and results must agree), once through the
 peer-memory exchange and once through NCCL all-to-all, over three successive
-calls (the peer-memory flags and buffers are reused across calls); the two
-exchanges must give bit-identical outputs.  Exits non-zero on any mismatch."""
+calls (the peer-memory flags and buffers are reused across calls) and, for
+the peer-memory path, two replays of a captured CUDA graph; the two exchanges
+must give bit-identical outputs.  Exits non-zero on any mismatch."""
 
 import datetime
 import os
@@ -64,6 +65,18 @@ def main():
                       f"rel_l2 vs single GPU {rel:.2e} {'ok' if good else 'MISMATCH'}", flush=True)
                 ok &= good
             outs[transport] = out.clone()
+            if ex is not None:
+                # the peer-memory path has no host sync: capture one call, replay it
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    g_out, _, _ = layer(x, full["router.weight"], full["router.bias"], local_p)
+                for rep in range(2):
+                    g.replay()
+                    torch.cuda.synchronize()
+                    same_g = torch.equal(g_out, outs[transport])
+                    print(f"rank {rank} {name} p2p graph replay {rep}: equal to eager {same_g}", flush=True)
+                    ok &= same_g
+                del g
             status = kernels.device_status(clear=True)
             if status:
                 print(f"rank {rank} {name} {transport}: device status {status}", flush=True)
