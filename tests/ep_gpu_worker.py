@@ -7,7 +7,9 @@ same library kernels, so routing and results must agree), once through the
 peer-memory exchange and once through NCCL all-to-all, over three successive
 calls (the peer-memory flags and buffers are reused across calls) and, for
 the peer-memory path, two replays of a captured CUDA graph; the two exchanges
-must give bit-identical outputs.  Exits non-zero on any mismatch."""
+must give bit-identical outputs.  Last, rank 0 calls the exchange while rank 1
+does not: rank 0's bounded waits must run out and report BS_ERR_TIMEOUT.
+Exits non-zero on any mismatch."""
 
 import datetime
 import os
@@ -19,7 +21,7 @@ import torch.distributed as dist
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path.insert(0, REPO)
 
-from blockstreamer_b200 import kernels  # noqa: E402
+from blockstreamer_b200 import _lib, kernels  # noqa: E402
 from blockstreamer_b200.expert_parallel import CudaOps, ExpertParallelMoE, P2PExchange, shard_experts  # noqa: E402
 from blockstreamer_b200.synthetic import CASES, LayerShape, make_layer, make_tokens  # noqa: E402
 
@@ -86,6 +88,26 @@ def main():
         same_bits = torch.equal(outs["p2p"], outs["nccl"])
         print(f"rank {rank} {name}: p2p and nccl outputs bit-identical: {same_bits}", flush=True)
         ok &= same_bits
+    # A peer that never takes part: rank 0 sends, rank 1 does not.  Rank 0's
+    # waits for rank 1's counts and rows run out (bounded, ~2 s each) and
+    # report BS_ERR_TIMEOUT through the status word; the context stays usable.
+    shape = cases[0][1]
+    ex = P2PExchange(None, shape.experts, shape.hidden, 64, shape.top_k, dev)
+    kernels.device_status(clear=True)
+    if rank == 0:
+        x0 = make_tokens(64, shape.hidden, 9, device=dev)
+        idx0 = torch.randint(0, shape.experts, (64, shape.top_k), device=dev, dtype=torch.int32)
+        d0 = kernels.dispatch(idx0, shape.experts)
+        ex.dispatch(x0, d0.expert_offsets, d0.token_of_row)
+        torch.cuda.synchronize()
+        status = kernels.device_status(clear=True)
+        alive = float(torch.ones(4, device=dev).sum().item()) == 4.0
+        timed_out = status == _lib.BS_ERR_TIMEOUT
+        print(f"rank 0 absent peer: device status {status} (timeout reported: {timed_out}), context usable: {alive}",
+              flush=True)
+        ok &= bool(timed_out) and alive
+    dist.barrier()
+    ex.close()
     flag = torch.tensor([0 if ok else 1], device=dev)
     dist.all_reduce(flag)
     dist.destroy_process_group()
