@@ -8,7 +8,8 @@ checkpoint exists offline); the weights (1.69 GB) are larger than L2, so no
 extra L2 flush is needed between steps.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload gptoss120b-prefill-8192|gptoss120b-decode-T|gptoss20b-prefill-4096]
+                  [--workload gptoss120b-prefill-8192|gptoss120b-decode-T|gptoss20b-prefill-4096|
+                              gptoss120b-zipf-16384-streamed]
 
 ``--impl reference`` times the reference's CPU path restated in ``oracle``
 (bf16 per-expert loop, the CPU baseline) on a bounded sample on rank 0.
@@ -39,6 +40,8 @@ L2_BYTES = 126 * 1024 * 1024
 
 
 def parse_workload(name: str):
+    if name.startswith("gptoss120b-zipf-"):   # gptoss120b-zipf-<T>-streamed
+        return "gptoss120b", 5, int(name.split("-")[2])
     if name.startswith("gptoss120b-prefill-"):
         return "gptoss120b", 4, int(name.rsplit("-", 1)[1])
     if name.startswith("gptoss120b-decode-"):
@@ -267,6 +270,8 @@ def run_ours(args, rank, world, local):
     key, case_id, T_total = parse_workload(args.workload)
     shape = CASES[key]
     dev = torch.device("cuda", torch.cuda.current_device())
+    if case_id == 5:
+        return run_bench_streamed(args, rank, world, shape, case_id, T_total)
     if world > 1:
         return run_bench_ep(args, rank, world, local, shape, case_id, T_total)
     T = T_total
@@ -570,6 +575,126 @@ def run_bench_ep(args, rank, world, local, shape, case_id, T_total):
     del graph
     if exchange is not None:
         exchange.close()
+
+
+# ---------------------------------------------------------------- streamed stack (config 5)
+
+def run_bench_streamed(args, rank, world, shape, case_id, T, layers=4, zipf_s=1.2):
+    """Config 5: a stack of ``layers`` B200GptOssMLP blocks whose expert
+    weights live in pinned host memory and stream into HBM through the
+    reference's own StreamedModel (prefetch_ahead=1, functional_call binding),
+    T tokens, router bias making expert popularity Zipf(s) over a seeded
+    expert permutation.  value = T * layers / step time (tokens through one
+    MoE layer per second); the host->device link bounds it."""
+    import types
+    if world > 1:
+        raise SystemExit("the streamed workload runs on one GPU")
+    ref_dir = os.path.join(REPO, "baseline", "_ref")
+    if not os.path.exists(os.path.join(ref_dir, "streamer.py")):
+        raise SystemExit("the streamed workload needs the reference package under baseline/_ref")
+    sys.path.insert(0, ref_dir)
+    from streamer import StreamedModel  # the reference's own streaming engine
+    from blockstreamer_b200 import B200GptOssMLP
+    from blockstreamer_b200.synthetic import zipf_router_bias
+
+    dev = torch.device("cuda", torch.cuda.current_device())
+    cfg = types.SimpleNamespace(hidden_size=shape.hidden, intermediate_size=shape.intermediate,
+                                num_local_experts=shape.experts, num_experts_per_tok=shape.top_k,
+                                swiglu_limit=7.0)
+    blocks = []
+    for layer in range(layers):
+        p = make_layer(shape, 10 * case_id + layer, device=dev)
+        p["router.bias"] = zipf_router_bias(shape, zipf_s, 10 * case_id + layer).to(dev)
+        mlp = B200GptOssMLP(cfg)
+        mlp.load_state_dict({n: t.cpu() for n, t in p.items()}, strict=True, assign=True)
+        blocks.append(mlp)
+        del p
+    torch.cuda.empty_cache()
+    x = make_tokens(T, shape.hidden, case_id, device=dev).view(1, T, shape.hidden)
+    hist = torch.bincount(kernels.router(x.view(T, -1), blocks[0].router.weight.to(dev),
+                                         blocks[0].router.bias.to(dev), shape.top_k)[2].reshape(-1).long(),
+                          minlength=shape.experts).cpu()
+    model = StreamedModel(blocks, device=dev, prefetch_ahead=1, dtype=None)
+    for _ in range(args.warmup):
+        model(x)
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream()
+    b0 = model.stats()["transfer_bytes"]
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        torch.cuda.synchronize()
+        ev0.record(st)
+        for _ in range(args.steps):
+            out, _ = model(x)
+        ev1.record(st)
+        torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    h2d_per_step = (model.stats()["transfer_bytes"] - b0) / args.steps
+    # the same blocks with every weight resident (compute alone), for the overlap
+    resident = [B200GptOssMLP(cfg) for _ in range(2)]
+    for r, b in zip(resident, blocks[:2]):
+        r.load_state_dict({n: t.to(dev) for n, t in b.state_dict().items()}, strict=True, assign=True)
+    for r in resident:
+        r(x)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(st)
+    for _ in range(args.steps):
+        for r in resident:
+            r(x)
+    b.record(st)
+    torch.cuda.synchronize()
+    compute_ms_layer = a.elapsed_time(b) / (args.steps * len(resident))
+    del resident
+    torch.cuda.empty_cache()
+    # host->device copy rate of pinned memory on this box (the bound)
+    src = torch.empty(1 << 30, dtype=torch.uint8).pin_memory()
+    dst = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
+    dst.copy_(src, non_blocking=True)
+    a.record(st)
+    for _ in range(3):
+        dst.copy_(src, non_blocking=True)
+    b.record(st)
+    torch.cuda.synchronize()
+    h2d_gbs = 3 * (1 << 30) / (a.elapsed_time(b) * 1e-3) / 1e9
+    del src, dst
+    # e2e: tokens in from pinned host memory, the stack's output back out
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty_like(x_host).pin_memory()
+    x_dev = torch.empty_like(x)
+    a.record(st)
+    for _ in range(args.steps):
+        x_dev.copy_(x_host, non_blocking=True)
+        o, _ = model(x_dev)
+        out_host.copy_(o, non_blocking=True)
+    b.record(st)
+    torch.cuda.synchronize()
+    e2e_ms = a.elapsed_time(b) / args.steps
+    achieved = h2d_per_step / (ms * 1e-3) / 1e9
+    line = {"metric": METRIC, "value": T * layers / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded weights, Zipf router bias)",
+            "config": {"workload": args.workload, "tokens": T, "layers": layers, "zipf_s": zipf_s,
+                       "streaming": "reference StreamedModel (baseline/_ref/streamer.py), prefetch_ahead=1, "
+                                    "pinned host weights, functional_call binding",
+                       "value_is": "tokens x layers / step time",
+                       "expert_rows_layer0_max_min": [int(hist.max()), int(hist.min())],
+                       "experts_hit_layer0": int((hist > 0).sum()),
+                       "l2": "inputs larger than L2 (1.69 GB of weights streamed per layer)"},
+            "roofline": {"bound": "host link", "achieved": achieved, "peak": h2d_gbs, "unit": "GB/s",
+                         "frac": achieved / h2d_gbs, "traffic": h2d_per_step,
+                         "kernel": "host->device weight streaming per step (all layers)",
+                         "peak_source": "measured pinned 1 GiB host->device copy on this box"},
+            "layer_roofline": {"compute_ms_per_layer_resident": compute_ms_layer,
+                               "h2d_ms_per_layer_at_peak": h2d_per_step / layers / (h2d_gbs * 1e9) * 1e3,
+                               "stream_ms_per_layer": ms / layers},
+            "e2e": {"value": T * layers / (e2e_ms * 1e-3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": x.numel() * 2,
+                    "api": "reference StreamedModel over blockstreamer_b200.B200GptOssMLP"},
+            "clocks": clk.summary(), "gpu_launches": 10 * layers * args.steps}
+    print(json.dumps(line), flush=True)
+    model.close()
 
 
 def main():

@@ -185,3 +185,42 @@ def test_drop_in_modules_bind_state_like_functional_call():
 
 def test_no_device_errors_recorded():
     assert kernels.device_status(clear=True) == 0
+
+
+def test_reference_streamed_model_streams_the_b200_mlp():
+    """The reference's own StreamedModel (installed under baseline/_ref)
+    streams B200GptOssMLP blocks from pinned host memory through its prefetch
+    ring (prefetch_ahead=1) and binds their state with functional_call: the
+    output equals running the same blocks resident on the GPU."""
+    import copy
+    import sys
+    import types
+
+    ref_dir = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
+    if not os.path.exists(os.path.join(ref_dir, "streamer.py")):
+        pytest.skip("reference package not installed under baseline/_ref")
+    if ref_dir not in sys.path:
+        sys.path.insert(0, ref_dir)
+    from streamer import StreamedModel
+    from blockstreamer_b200 import B200GptOssMLP
+
+    shape = LayerShape(512, 512, 16, 4)
+    cfg = types.SimpleNamespace(hidden_size=shape.hidden, intermediate_size=shape.intermediate,
+                                num_local_experts=shape.experts, num_experts_per_tok=shape.top_k,
+                                swiglu_limit=7.0)
+    blocks = []
+    for layer in range(3):
+        mlp = B200GptOssMLP(cfg)
+        mlp.load_state_dict(make_layer(shape, 20 + layer), strict=True, assign=True)
+        blocks.append(mlp)
+    resident = [copy.deepcopy(b).to(DEV) for b in blocks]
+    x = make_tokens(96, shape.hidden, 20).to(DEV).reshape(3, 32, shape.hidden)
+    h = x
+    for b in resident:
+        h, scores_direct = b(h)
+    model = StreamedModel(blocks, device=DEV, prefetch_ahead=1, dtype=None)
+    out, scores = model(x)
+    torch.cuda.synchronize()
+    assert torch.equal(out, h)
+    assert torch.equal(scores, scores_direct)
+    assert model.stats()["transfer_bytes"] > 0
