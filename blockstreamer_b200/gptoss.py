@@ -77,6 +77,37 @@ def mxfp4_matmul(x: Tensor, blocks: Tensor, scales: Tensor) -> Tensor:
     return _MXFP4Matmul.apply(x, blocks, scales)
 
 
+def _apply_gate(gate_up: Tensor, limit: float, alpha: float) -> Tensor:
+    """gptoss.py:130-135: clamped, interleaved SwiGLU in the tensor's dtype."""
+    gate = gate_up[..., ::2].clamp(max=limit)
+    up = gate_up[..., 1::2].clamp(min=-limit, max=limit)
+    return (up + 1) * (gate * torch.sigmoid(gate * alpha))
+
+
+def _experts_autograd(m: "B200MXFP4Experts", hidden: Tensor, indices: Tensor, weights: Tensor) -> Tensor:
+    """The expert loop of gptoss.py:137-177, step for step, for when gradients
+    are needed (dL/dx and dL/d routing weights): per hit expert, the fused
+    dequant-GEMM forward of ``mxfp4_matmul`` and, in backward, the dense weight
+    re-derived by the dequant kernel (gptoss.py:64-71).  Like the reference it
+    synchronizes with the host to find the hit experts and their rows."""
+    E = m.num_experts
+    next_states = torch.zeros_like(hidden)
+    with torch.no_grad():
+        mask = torch.nn.functional.one_hot(indices.long(), num_classes=E).permute(2, 1, 0)
+        hit = torch.greater(mask.sum(dim=(-1, -2)), 0).nonzero()
+    for entry in hit:
+        e = int(entry[0])
+        top_k_pos, token_idx = torch.where(mask[e])
+        current = hidden[token_idx]
+        gate_up = mxfp4_matmul(current, m.gate_up_proj_blocks[e:e + 1], m.gate_up_proj_scales[e:e + 1]) \
+            + m.gate_up_proj_bias[e]
+        gated = _apply_gate(gate_up, m.limit, m.alpha)
+        out = mxfp4_matmul(gated, m.down_proj_blocks[e:e + 1], m.down_proj_scales[e:e + 1]) + m.down_proj_bias[e]
+        out = out * weights[token_idx, top_k_pos, None]
+        next_states = next_states.index_add(0, token_idx, out.to(hidden.dtype))
+    return next_states
+
+
 def _packed(experts: int, rows: int, groups: int) -> nn.Parameter:
     return nn.Parameter(torch.empty(experts, rows, groups, 16, dtype=torch.uint8, device="meta"),
                         requires_grad=False)
@@ -119,6 +150,8 @@ class B200MXFP4Experts(nn.Module):
                 routing_weights: Tensor | None = None) -> Tensor:
         if router_indices is None or routing_weights is None:
             raise ValueError("B200MXFP4Experts needs router_indices and routing_weights")
+        if torch.is_grad_enabled() and (hidden_states.requires_grad or routing_weights.requires_grad):
+            return _experts_autograd(self, hidden_states, router_indices, routing_weights)
         k = router_indices.shape[-1]
         out, _, _ = kernels.moe_forward(
             hidden_states.to(torch.bfloat16), self.gate_up_proj_blocks, self.gate_up_proj_scales,
@@ -155,8 +188,18 @@ class B200GptOssMLP(nn.Module):
 
     def forward(self, hidden_states: Tensor):
         B, S, H = hidden_states.shape
-        x = hidden_states.reshape(-1, H).to(torch.bfloat16)
         ex = self.experts
+        if torch.is_grad_enabled() and hidden_states.requires_grad:
+            # differentiable form: the HF router (modeling_gpt_oss.py:126-130)
+            # in torch ops, then the expert loop above
+            flat = hidden_states.reshape(-1, H)
+            logits = torch.nn.functional.linear(flat.to(self.router.weight.dtype), self.router.weight,
+                                                self.router.bias)
+            top_v, top_i = torch.topk(logits, self.top_k, dim=-1)
+            scores = torch.softmax(top_v, dim=1, dtype=top_v.dtype)
+            out = _experts_autograd(ex, flat, top_i, scores)
+            return out.reshape(B, S, H), scores
+        x = hidden_states.reshape(-1, H).to(torch.bfloat16)
         out, scores, _ = kernels.moe_forward(
             x, ex.gate_up_proj_blocks, ex.gate_up_proj_scales, ex.gate_up_proj_bias,
             ex.down_proj_blocks, ex.down_proj_scales, ex.down_proj_bias, self.top_k,

@@ -224,3 +224,54 @@ def test_reference_streamed_model_streams_the_b200_mlp():
     assert torch.equal(out, h)
     assert torch.equal(scores, scores_direct)
     assert model.stats()["transfer_bytes"] > 0
+
+
+def test_experts_and_mlp_backward_match_fp32_autograd():
+    """Gradients through the drop-in modules (the reference trains through the
+    experts: gptoss.py:45-75, 137-177): dL/dx and dL/d routing weights of
+    B200MXFP4Experts, and dL/dx of B200GptOssMLP (router included), against
+    autograd through the fp32 restatement of the reference math."""
+    import types
+    from blockstreamer_b200 import B200GptOssMLP, B200MXFP4Experts
+
+    shape = CASES["tiny"]
+    cfg = types.SimpleNamespace(hidden_size=shape.hidden, intermediate_size=shape.intermediate,
+                                num_local_experts=shape.experts, num_experts_per_tok=shape.top_k,
+                                swiglu_limit=7.0)
+    p = make_layer(shape, 3)
+    x = make_tokens(64, shape.hidden, 3)
+    pe = experts_of(p)
+    _, s_ref, i_ref = omoe.router(x.float(), p["router.weight"], p["router.bias"], shape.top_k)
+    g = torch.randn(64, shape.hidden, generator=torch.Generator().manual_seed(5))
+
+    ex = B200MXFP4Experts(cfg)
+    ex.load_state_dict({n: t.to(DEV) for n, t in pe.items()}, strict=True, assign=True)
+    xg = x.to(DEV).float().requires_grad_()
+    wg = s_ref.to(DEV).requires_grad_()
+    out = ex(xg, i_ref.to(DEV), wg)
+    out.backward(g.to(DEV))
+    xc = x.float().requires_grad_()
+    wc = s_ref.clone().requires_grad_()
+    ref = omoe.experts_fp32(xc, i_ref, wc, pe)
+    ref.backward(g)
+    r_out, r_dx, r_dw = (omoe.rel_l2(out.detach().cpu(), ref.detach()), omoe.rel_l2(xg.grad.cpu(), xc.grad),
+                         omoe.rel_l2(wg.grad.cpu(), wc.grad))
+    print(f"experts: out {r_out:.2e} dx {r_dx:.2e} dw {r_dw:.2e}")
+    assert r_out <= 5e-3 and r_dx <= 1e-2 and r_dw <= 1e-2
+
+    mlp = B200GptOssMLP(cfg)
+    mlp.load_state_dict({n: t.to(DEV) for n, t in p.items()}, strict=True, assign=True)
+    xm = x.to(DEV).float().reshape(2, 32, shape.hidden).requires_grad_()
+    om, _ = mlp(xm)
+    om.reshape(64, -1).backward(g.to(DEV))
+    xr = x.float().requires_grad_()
+    logits = torch.nn.functional.linear(xr, p["router.weight"], p["router.bias"])
+    top_v, top_i = torch.topk(logits, shape.top_k, dim=-1)
+    ref_m = omoe.experts_fp32(xr, top_i, torch.softmax(top_v, dim=1), pe)
+    ref_m.backward(g)
+    keep = ~omoe.near_tie_tokens(omoe.router_logits_f64(x, p["router.weight"], p["router.bias"]),
+                                 shape.top_k, 1e-6 + omoe.ROUTER_LOGIT_ERR, logits.detach())
+    r_mo = omoe.rel_l2(om.detach().reshape(64, -1).cpu()[keep], ref_m.detach()[keep])
+    r_mdx = omoe.rel_l2(xm.grad.reshape(64, -1).cpu()[keep], xr.grad[keep])
+    print(f"mlp: out {r_mo:.2e} dx {r_mdx:.2e}")
+    assert r_mo <= 5e-3 and r_mdx <= 1e-2
