@@ -53,9 +53,6 @@ SIGNATURES = {
     "bs_ep_p2p_free": (_i32, [_vp]),
     "bs_ep_p2p_dispatch": (_i32, [_vp, _i64, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp]),
     "bs_ep_p2p_return": (_i32, [_vp, _i64, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _vp]),
-    "bs_ep_p2p_targets": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp, _vp]),
-    "bs_ep_p2p_results_sent": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _vp]),
-    "bs_moe_down_rows": (_i32, [_vp, _vp, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _i32, _vp, _vp]),
     "bs_combine": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp]),
     "bs_mxfp4_matmul": (_i32, [_vp, _i64, _i64, _vp, _vp, _i64, _vp, _vp, _i32, _vp]),
     "bs_moe_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64]),

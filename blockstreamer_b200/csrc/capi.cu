@@ -26,8 +26,7 @@ int gemv_plain_launch(const void* x, const int32_t* offsets, int64_t rows_total,
 int tc_grouped_launch(int mode, const void* x, const int32_t* offsets, int64_t rows_total,
                       int64_t max_rows_per_expert, int64_t E, int64_t K, int64_t N,
                       const void* blocks, const void* scales, const void* bias, int bias_f32,
-                      float alpha, float limit, void* out, cudaStream_t st,
-                      const uint64_t* row_dst = nullptr);
+                      float alpha, float limit, void* out, cudaStream_t st);
 bool tc_supported(const void* scales, int64_t K, int64_t N);
 // Decode path (decode.cu): router + dispatch + block-scaled expert MMAs + combine, T <= 64.
 bool decode_supported(int64_t T, int64_t H, int64_t I, int64_t E, int64_t k);
@@ -158,20 +157,6 @@ extern "C" int bs_moe_down(const void* h, const int32_t* expert_offsets, int64_t
                            void* y, int algo, void* stream) {
   return bs::down(h, expert_offsets, rows_total, max_rows_per_expert, E, H, I, blocks, scales, bias,
                   bias_dtype, y, algo, reinterpret_cast<cudaStream_t>(stream));
-}
-
-extern "C" int bs_moe_down_rows(const void* h, const int32_t* expert_offsets, int64_t rows_total, int64_t E,
-                                int64_t H, int64_t I, const void* blocks, const void* scales,
-                                const void* bias, int bias_dtype, const uint64_t* row_dst, void* stream) {
-  using namespace bs;
-  BS_TRY(check_expert_args("bs_moe_down_rows", h, blocks, scales, row_dst, rows_total, E, I, H, bias_dtype,
-                           BS_ALGO_TCGEN05));
-  BS_ARG(expert_offsets, "bs_moe_down_rows: null expert_offsets");
-  if (rows_total == 0) return BS_OK;
-  BS_TRY(check_device());
-  return tc_grouped_launch(1, h, expert_offsets, rows_total, rows_total, E, I, H, blocks, scales, bias,
-                           bias_dtype == BS_F32, 0.f, 0.f, nullptr, reinterpret_cast<cudaStream_t>(stream),
-                           row_dst);
 }
 
 extern "C" int bs_mxfp4_matmul(const void* x, int64_t m, int64_t K, const void* blocks,

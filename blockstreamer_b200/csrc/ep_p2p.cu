@@ -260,59 +260,6 @@ __global__ void __launch_bounds__(256) ep_return_kernel(const uint4* __restrict_
   }
 }
 
-// For each row r of recv (expert-major): the address of its result row in the
-// source rank's yback, so that the down projection's epilogue can store it
-// there directly (bs_moe_down_rows).  Same tables as ep_return_kernel.
-__global__ void __launch_bounds__(256) ep_targets_kernel(const uint64_t* __restrict__ bases, int R, int E,
-                                                         int me, int64_t row_bytes, EPLayout L,
-                                                         uint64_t* __restrict__ row_dst) {
-  extern __shared__ int sm[];
-  const int El = E / R;
-  int* cm = sm;
-  int* loc = cm + R * E;
-  int* seg = loc + El + 1;
-  int* src = seg + El * (R + 1);
-  const volatile int* cmg = at<int>(bases[me], L.counts);
-  for (int i = threadIdx.x; i < R * E; i += blockDim.x) cm[i] = cmg[i];
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int run = 0;
-    for (int e = 0; e < El; ++e) {
-      loc[e] = run;
-      int rs = 0;
-      for (int s = 0; s < R; ++s) {
-        seg[e * (R + 1) + s] = rs;
-        rs += cm[s * E + me * El + e];
-      }
-      seg[e * (R + 1) + R] = rs;
-      run += rs;
-    }
-    loc[El] = run;
-  }
-  for (int i = threadIdx.x; i < El * R; i += blockDim.x) {
-    const int e = i / R, s = i - e * R;
-    int p = 0;
-    for (int e2 = 0; e2 < me * El + e; ++e2) p += cm[s * E + e2];
-    src[e * R + s] = p;
-  }
-  __syncthreads();
-  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < loc[El]; r += gridDim.x * blockDim.x) {
-    const int e = last_le(loc, El + 1, r);
-    const int within = r - loc[e];
-    const int s = last_le(seg + e * (R + 1), R + 1, within);
-    const int64_t dst_row = src[e * R + s] + (within - seg[e * (R + 1) + s]);
-    row_dst[r] = bases[s] + L.yback + (uint64_t)(dst_row * row_bytes);
-  }
-}
-
-// After the down projection stored its rows into the sources' yback: raise
-// flags.results[me] on every rank.
-__global__ void ep_signal_kernel(const uint64_t* __restrict__ bases, int R, int me, EPLayout L) {
-  const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(at<uint32_t>(bases[me], L.flags) + kEpoch);
-  __threadfence_system();
-  if ((int)threadIdx.x < R) st_release_sys(at<uint32_t>(bases[threadIdx.x], L.flags) + kResults * kMaxRanks + me, epoch);
-}
-
 int check_shape(int64_t R, int64_t E, int64_t H, int64_t me) {
   BS_TRY(check_device());
   BS_ARG(R >= 1 && R <= kMaxRanks, "expert parallel: 1 <= ranks <= %d", kMaxRanks);
@@ -423,36 +370,6 @@ int bs_ep_p2p_return(const void* y, int64_t H, void* my_base, const uint64_t* pe
   BS_CUDA(cudaGetLastError());
   ep_arrived_kernel<<<1, 32, 0, st>>>(reinterpret_cast<uint64_t>(my_base), L, kResults, (int)R, (int)E, (int)me, 0,
                                       nullptr, status);
-  BS_CUDA(cudaGetLastError());
-  return BS_OK;
-}
-
-int bs_ep_p2p_targets(void* my_base, const uint64_t* peer_bases, int64_t R, int64_t E, int64_t H, int64_t me,
-                      int64_t cap_rows, int64_t src_rows, uint64_t* row_dst, void* stream) {
-  BS_TRY(check_shape(R, E, H, me));
-  BS_ARG(my_base && peer_bases && row_dst, "bs_ep_p2p_targets: null pointer");
-  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const EPLayout L = ep_layout(R, E, H, cap_rows, src_rows);
-  const int El = (int)(E / R);
-  const size_t smem = (size_t)(R * E + (El + 1) + El * (R + 1) + El * R) * 4;
-  BS_REQUIRE(smem <= 48 * 1024, BS_ERR_UNSUPPORTED, "bs_ep_p2p_targets: %lld ranks x %lld experts too large",
-             (long long)R, (long long)E);
-  const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((cap_rows + 255) / 256, sm_count()));
-  ep_targets_kernel<<<grid, 256, smem, st>>>(peer_bases, (int)R, (int)E, (int)me, H * 2, L, row_dst);
-  BS_CUDA(cudaGetLastError());
-  return BS_OK;
-}
-
-int bs_ep_p2p_results_sent(void* my_base, const uint64_t* peer_bases, int64_t R, int64_t E, int64_t H, int64_t me,
-                           int64_t cap_rows, int64_t src_rows, void* stream) {
-  BS_TRY(check_shape(R, E, H, me));
-  BS_ARG(my_base && peer_bases, "bs_ep_p2p_results_sent: null pointer");
-  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const EPLayout L = ep_layout(R, E, H, cap_rows, src_rows);
-  ep_signal_kernel<<<1, 64, 0, st>>>(peer_bases, (int)R, (int)me, L);
-  BS_CUDA(cudaGetLastError());
-  ep_arrived_kernel<<<1, 32, 0, st>>>(reinterpret_cast<uint64_t>(my_base), L, kResults, (int)R, (int)E, (int)me, 0,
-                                      nullptr, device_status_ptr());
   BS_CUDA(cudaGetLastError());
   return BS_OK;
 }

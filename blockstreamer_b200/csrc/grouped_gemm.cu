@@ -134,13 +134,10 @@ __device__ __forceinline__ float swiglu_fast(float gate, float up, float alpha, 
 // One 16-column chunk of the accumulator (one token per column) for the lane's
 // weight row: bias, then SwiGLU across the (gate, up) lane pair (MODE 0) or the
 // plain projection (MODE 1), stored as bf16.
-// MODE 1 with row_dst: row r of the result goes to the address row_dst[r]
-// (a row of another GPU's buffer, mapped over NVLink) instead of out + r * Nw.
 template <int MODE>
 __device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[16], int c0, const Tile& t, int row_w,
                                                bool rv, float bv, float bp, int lane, int Nw,
-                                               float alpha, float limit, uint16_t* __restrict__ out,
-                                               const uint64_t* __restrict__ row_dst) {
+                                               float alpha, float limit, uint16_t* __restrict__ out) {
   if (MODE == 0) {
     // Lane pair (2i, 2i+1) holds the gate and up rows of one output column.
     // The even lane produces the pair's even token columns, the odd lane the
@@ -160,14 +157,6 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[16], int c0, 
       const int n = c0 + 2 * jj + odd;
       if (n < t.nrows && rv) orow[(t.r0 + n) * Iout] = __bfloat16_as_ushort(__float2bfloat16_rn(hv));
     }
-  } else if (row_dst) {
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const int n = c0 + i;
-      if (n < t.nrows && rv)
-        reinterpret_cast<uint16_t*>(row_dst[t.r0 + n])[row_w] =
-            __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[i]) + bv));
-    }
   } else {
     uint16_t* ocol = out + row_w;
 #pragma unroll
@@ -184,7 +173,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_kernel(
     const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_a,
     const uint8_t* __restrict__ scales, const int* __restrict__ offsets, int64_t rows_total,
     int E, int K, int Nw, const void* __restrict__ bias, int bias_f32, float alpha, float limit,
-    uint16_t* __restrict__ out, const uint64_t* __restrict__ row_dst, int* status) {
+    uint16_t* __restrict__ out, int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -387,15 +376,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_kernel(
         uint32_t v[16];
         ptx::tmem_ld_32x32b_x16(taddr + c0, v);
         ptx::tmem_wait_ld();
-        epilogue_chunk<MODE>(v, c0, t, row_w, rv, bv, bp, lane, Nw, alpha, limit, out, row_dst);
+        epilogue_chunk<MODE>(v, c0, t, row_w, rv, bv, bp, lane, Nw, alpha, limit, out);
       }
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(accempty);
     }
-    // stores to other GPUs: make them visible system-wide before the kernel
-    // that raises the peers' flags (stream-ordered after this one)
-    if (row_dst) __threadfence_system();
   } else {
     // ------------------------------------------------------------ dequant (A -> TMEM)
     const int dg = (warp - kWarpDeq0) >> 2;  // dequant group: takes K steps ks = dg, dg+2, ...
@@ -461,9 +447,8 @@ bool tc_supported(const void* scales, int64_t K, int64_t N) {
 int tc_grouped_launch(int mode, const void* x, const int32_t* offsets, int64_t rows_total,
                       int64_t max_rows_per_expert, int64_t E, int64_t K, int64_t N,
                       const void* blocks, const void* scales, const void* bias, int bias_f32,
-                      float alpha, float limit, void* out, cudaStream_t st, const uint64_t* row_dst) {
+                      float alpha, float limit, void* out, cudaStream_t st) {
   (void)max_rows_per_expert;
-  BS_ARG(!row_dst || mode == 1, "tcgen05 GEMM: row destinations only for the down projection");
   BS_ARG(E * N < (int64_t)INT32_MAX && rows_total + kNMax < (int64_t)INT32_MAX,
          "tcgen05 GEMM: sizes exceed 32-bit TMA coordinates");
   BS_ARG(mode == 1 || N % 2 == 0, "tcgen05 GEMM: gate_up rows must be even");
@@ -486,7 +471,7 @@ int tc_grouped_launch(int mode, const void* x, const int32_t* offsets, int64_t r
   const int grid = sm_count();
   kern<<<grid, kThreads, smem, st>>>(tm_b, tm_a, static_cast<const uint8_t*>(scales), offsets,
                                      rows_total, (int)E, (int)K, (int)N, bias, bias_f32, alpha,
-                                     limit, static_cast<uint16_t*>(out), row_dst, device_status_ptr());
+                                     limit, static_cast<uint16_t*>(out), device_status_ptr());
   BS_LAUNCHED();
   return BS_OK;
 }

@@ -133,7 +133,6 @@ class P2PExchange:
         self.yback = raw[yo.value: yo.value + self.src_rows * self.H * 2].view(torch.bfloat16).view(
             self.src_rows, self.H)
         self.local_offsets = torch.zeros(self.E // self.R + 1, dtype=torch.int32, device=self.device)
-        self.row_dst = torch.zeros(self.cap, dtype=torch.int64, device=self.device)
         self._closed = False
 
     def dispatch(self, x: torch.Tensor, expert_offsets: torch.Tensor, token_of_row: torch.Tensor):
@@ -149,20 +148,6 @@ class P2PExchange:
             _lib.call("bs_ep_p2p_return", y.data_ptr(), self.H, self.base, self.bases.data_ptr(), self.R,
                       self.E, self.me, self.cap, self.src_rows,
                       torch.cuda.current_stream(self.device).cuda_stream)
-
-    def targets(self):
-        """row_dst[r] = address of recv row r's result row in its source's yback."""
-        with torch.cuda.device(self.device):
-            _lib.call("bs_ep_p2p_targets", self.base, self.bases.data_ptr(), self.R, self.E, self.H, self.me,
-                      self.cap, self.src_rows, self.row_dst.data_ptr(),
-                      torch.cuda.current_stream(self.device).cuda_stream)
-
-    def results_sent(self):
-        """After bs_moe_down_rows stored every result row: signal the sources and
-        wait for every rank's results to this rank."""
-        with torch.cuda.device(self.device):
-            _lib.call("bs_ep_p2p_results_sent", self.base, self.bases.data_ptr(), self.R, self.E, self.H,
-                      self.me, self.cap, self.src_rows, torch.cuda.current_stream(self.device).cuda_stream)
 
     def close(self):
         """Collective: unmap the peers, then free this rank's buffer."""
@@ -191,7 +176,7 @@ class ExpertParallelMoE:
 
     def __init__(self, num_experts: int, top_k: int, group=None, ops=None,
                  alpha: float = kernels.ALPHA, limit: float = kernels.LIMIT,
-                 exchange: P2PExchange | None = None, fused_return: bool = False):
+                 exchange: P2PExchange | None = None):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -205,12 +190,6 @@ class ExpertParallelMoE:
         self.last_stats: EPStats | None = None
         # peer-memory exchange (GPUs); None: NCCL / gloo all-to-all
         self.exchange = exchange
-        # peer-memory path: with fused_return the down projection's epilogue
-        # stores each result row straight into its source's buffer (tcgen05
-        # form); by default it writes locally and a copy kernel sends the rows
-        # back, which measured faster (2 GPUs: 1.14 vs 1.23 ms per layer): the
-        # epilogue's remote stores are 64 bytes per warp instruction and stall it
-        self.fused_return = fused_return
         self._h = self._y = None
         # optional: a list that receives (stage name, CUDA event) at stage ends
         self.marks: list | None = None
@@ -279,21 +258,12 @@ class ExpertParallelMoE:
             self._h = torch.empty(ex.cap, I, dtype=torch.bfloat16, device=x.device)
             self._y = torch.empty(ex.cap, H, dtype=torch.bfloat16, device=x.device)
         algo = getattr(self.ops, "algo", kernels.ALGO_AUTO)
-        fused = self.fused_return and algo in (kernels.ALGO_AUTO, kernels.ALGO_TCGEN05)
-        if fused:
-            ex.targets()
         kernels.moe_gate_up(ex.recv, ex.local_offsets, p["gate_up_proj_blocks"], p["gate_up_proj_scales"],
                             p["gate_up_proj_bias"], alpha=self.alpha, limit=self.limit, algo=algo, out=self._h)
-        if fused:
-            kernels.moe_down_rows(self._h, ex.local_offsets, p["down_proj_blocks"], p["down_proj_scales"],
-                                  p["down_proj_bias"], ex.row_dst)
-            self._mark("experts")
-            ex.results_sent()
-        else:
-            kernels.moe_down(self._h, ex.local_offsets, p["down_proj_blocks"], p["down_proj_scales"],
-                             p["down_proj_bias"], algo=algo, out=self._y)
-            self._mark("experts")
-            ex.give_back(self._y)
+        kernels.moe_down(self._h, ex.local_offsets, p["down_proj_blocks"], p["down_proj_scales"],
+                         p["down_proj_bias"], algo=algo, out=self._y)
+        self._mark("experts")
+        ex.give_back(self._y)
         self._mark("exchange_combine")
         out = kernels.combine(ex.yback[: T * k], d.row_of_slot, sc, T)
         self._mark("combine")

@@ -202,19 +202,6 @@ def moe_down(h, expert_offsets, blocks, scales, bias, algo=ALGO_AUTO, max_rows_p
     return y
 
 
-def moe_down_rows(h, expert_offsets, blocks, scales, bias, row_dst: torch.Tensor) -> None:
-    """Down projection whose result row r is stored at the address row_dst[r]
-    (see bs_moe_down_rows): the expert-parallel layer's fused return."""
-    _cuda("moe_down_rows", h, expert_offsets, blocks, scales, bias, row_dst)
-    S, I = h.shape
-    E, H, G, _ = blocks.shape
-    if G * 32 != I or row_dst.numel() < S:
-        raise ValueError("moe_down_rows: shapes do not match")
-    with torch.cuda.device(h.device):
-        _lib.call("bs_moe_down_rows", _p(h), _p(expert_offsets), S, E, H, I, _p(blocks), _p(scales),
-                  _p(bias), _bias_code(bias), _p(row_dst), _stream(h))
-
-
 def combine(y: torch.Tensor, row_of_slot: torch.Tensor, weights: torch.Tensor, num_tokens: int,
             out: torch.Tensor | None = None) -> torch.Tensor:
     """out[t] = sum_s weights[t,s] * y[row_of_slot[t*k+s]] (fp32 sum, bf16 out)."""

@@ -162,16 +162,6 @@ int bs_ep_regroup(const int32_t* recv_counts, int64_t R, int64_t El, const void*
                   int64_t rows, int64_t H, void* x_grouped, int32_t* expert_offsets,
                   int32_t* row_map, void* stream);
 
-/* bs_moe_down (tcgen05 form) whose result row r is stored at the address
- * row_dst[r] (H bf16, 16-byte aligned rows; typically rows of other GPUs'
- * buffers mapped over NVLink, from bs_ep_p2p_targets) instead of y + r*H.
- * Replaces gptoss.py:167-174 for the expert-parallel layer, fused with the
- * return half of its exchange; rows_total bounds the rows addressed by the
- * expert offsets.  No counterpart in the reference (no distributed backend). */
-int bs_moe_down_rows(const void* h, const int32_t* expert_offsets, int64_t rows_total, int64_t E,
-                     int64_t H, int64_t I, const void* blocks, const void* scales, const void* bias,
-                     int bias_dtype, const uint64_t* row_dst, void* stream);
-
 /* dst[i] = src[row_map[i]] for i < rows, rows of H bf16 (undoes bs_ep_regroup). */
 int bs_gather_rows(const void* src, const int32_t* row_map, int64_t rows, int64_t H, void* dst,
                    void* stream);
@@ -220,19 +210,6 @@ int bs_ep_p2p_dispatch(const void* x, int64_t H, const int32_t* expert_offsets,
 int bs_ep_p2p_return(const void* y, int64_t H, void* my_base, const uint64_t* peer_bases,
                      int64_t R, int64_t E, int64_t me, int64_t cap_rows, int64_t src_rows,
                      void* stream);
-/* The fused return: instead of the down projection writing results [cap_rows, H]
- * and bs_ep_p2p_return copying them back, bs_ep_p2p_targets writes, for each
- * row of recv, the address of its result row in its source rank's yback
- * (row_dst [cap_rows] u64, after bs_ep_p2p_dispatch on the stream);
- * bs_moe_down_rows then stores every result row straight there over NVLink
- * from its epilogue, and bs_ep_p2p_results_sent raises this rank's flags and
- * waits (bounded) for every other rank's results, like the end of
- * bs_ep_p2p_return. */
-int bs_ep_p2p_targets(void* my_base, const uint64_t* peer_bases, int64_t R, int64_t E, int64_t H,
-                      int64_t me, int64_t cap_rows, int64_t src_rows, uint64_t* row_dst,
-                      void* stream);
-int bs_ep_p2p_results_sent(void* my_base, const uint64_t* peer_bases, int64_t R, int64_t E,
-                           int64_t H, int64_t me, int64_t cap_rows, int64_t src_rows, void* stream);
 
 /* One expert projection without activation: out[m, N] = x[m, K] @ dequant(W) (+ bias).
  * Replaces block_streamer/gptoss.py:74-75 (mxfp4_matmul forward) for one expert:

@@ -4,9 +4,7 @@ from tests/test_gpu_ep.py; not collected by pytest).
 Each rank owns E/R experts and T/R tokens.  For each case the layer output of
 the rank's tokens is compared with the single-GPU layer on all tokens (the
 same library kernels, so routing and results must agree), once through the
-peer-memory exchange (results stored by the down projection's epilogue
-straight into the sources' buffers, and, separately, copied back by a kernel)
-and once through NCCL all-to-all, over three successive
+peer-memory exchange and once through NCCL all-to-all, over three successive
 calls (the peer-memory flags and buffers are reused across calls) and, for
 the peer-memory path, two replays of a captured CUDA graph; the two exchanges
 must give bit-identical outputs.  Last, rank 0 calls the exchange while rank 1
@@ -56,11 +54,9 @@ def main():
         x = x_all[sl].contiguous()
         local_p = shard_experts(pe, rank, world)
         outs = {}
-        for transport in ("p2p", "p2p_copy", "nccl"):
-            ex = P2PExchange(None, shape.experts, shape.hidden, Tr, shape.top_k, dev) \
-                if transport.startswith("p2p") else None
-            layer = ExpertParallelMoE(shape.experts, shape.top_k, ops=CudaOps(algo), exchange=ex,
-                                      fused_return=transport == "p2p")
+        for transport in ("p2p", "nccl"):
+            ex = P2PExchange(None, shape.experts, shape.hidden, Tr, shape.top_k, dev) if transport == "p2p" else None
+            layer = ExpertParallelMoE(shape.experts, shape.top_k, ops=CudaOps(algo), exchange=ex)
             for call in range(3):
                 out, _, idx = layer(x, full["router.weight"], full["router.bias"], local_p)
                 torch.cuda.synchronize()
@@ -89,9 +85,8 @@ def main():
                 ok = False
             if ex is not None:
                 ex.close()
-        same_bits = torch.equal(outs["p2p"], outs["nccl"]) and torch.equal(outs["p2p_copy"], outs["nccl"])
-        print(f"rank {rank} {name}: p2p (fused return), p2p (copy return) and nccl outputs bit-identical: "
-              f"{same_bits}", flush=True)
+        same_bits = torch.equal(outs["p2p"], outs["nccl"])
+        print(f"rank {rank} {name}: p2p and nccl outputs bit-identical: {same_bits}", flush=True)
         ok &= same_bits
     # A peer that never takes part: rank 0 sends, rank 1 does not.  Rank 0's
     # waits for rank 1's counts and rows run out (bounded, ~2 s each) and
