@@ -88,3 +88,24 @@ def test_workspace_size_formula():
 def test_python_raises_valueerror_with_message():
     with pytest.raises(ValueError, match="null pointer"):
         _lib.call("bs_dequant_mxfp4", None, None, 1, 1, 1, 1, None, None)
+
+
+def test_expert_parallel_exchange_layout():
+    """bs_ep_p2p_bytes / bs_ep_p2p_layout (host arithmetic, no GPU): the receive
+    area holds cap_rows rows and the result area src_rows rows, 256-byte aligned
+    and disjoint, inside the buffer; argument checks reject bad rank/expert
+    counts before any device work."""
+    lib = _lib.load()
+    for R, E, H, T, k in ((2, 128, 2880, 4096, 4), (8, 128, 2880, 1024, 4), (4, 16, 512, 64, 2)):
+        src_rows = T * k
+        cap = R * src_rows
+        total = lib.bs_ep_p2p_bytes(R, E, H, cap, src_rows)
+        ro, yo = ctypes.c_size_t(), ctypes.c_size_t()
+        assert lib.bs_ep_p2p_layout(R, E, H, cap, src_rows, ctypes.byref(ro), ctypes.byref(yo)) == 0
+        assert ro.value % 256 == 0 and yo.value % 256 == 0
+        assert ro.value >= R * E * 4                       # flags and the counts matrix come first
+        assert yo.value >= ro.value + cap * H * 2           # recv, then yback
+        assert total >= yo.value + src_rows * H * 2
+    base = ctypes.c_void_p(16)
+    st = lib.bs_ep_p2p_dispatch(base, 2880, base, base, base, base, 3, 128, 0, 3, 1, base, None)
+    assert st == _lib.BS_ERR_INVALID_ARGUMENT or st == _lib.BS_ERR_UNSUPPORTED   # 128 experts over 3 ranks
