@@ -388,7 +388,7 @@ def run_ours(args, rank, world, local):
             ready.record(s_in)
         st.wait_event(ready)
         o, _, _ = kernels.moe_forward(x_dev[b], *gu, *dn, k, router_weight=p["router.weight"],
-                                      router_bias=p["router.bias"], algo=algo, workspace=ws)
+                                      router_bias=p["router.bias"], algo=algo)
         done = torch.cuda.Event()
         done.record(st)
         comp_done[b] = done
