@@ -548,21 +548,61 @@ def run_bench_ep(args, rank, world, local, shape, case_id, T_total):
     layer.marks = None
     # e2e: this rank's tokens in from pinned host memory, its output back out
     x_host = x.cpu().pin_memory()
-    out_host = torch.empty_like(x_host).pin_memory()
-    x_dev = x if graph is not None else torch.empty_like(x)   # the graph's input buffer
-    e2e = []
-    for i in range(args.warmup + args.steps):
+    if exchange is not None:
+        # peer-memory path (no host sync): copies on their own streams,
+        # double-buffered, overlapping the layer as in the single-GPU e2e; the
+        # ranks stay in step through the exchange's device flags
+        out_host = [torch.empty_like(x_host).pin_memory() for _ in range(2)]
+        x_dev = [torch.empty_like(x) for _ in range(2)]
+        s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+        comp_done = [None, None]
+
+        def e2e_step(i, first_event=None):
+            b = i % 2
+            with torch.cuda.stream(s_in):
+                if comp_done[b] is not None:
+                    s_in.wait_event(comp_done[b])
+                if first_event is not None:
+                    first_event.record(s_in)
+                x_dev[b].copy_(x_host, non_blocking=True)
+                ready = torch.cuda.Event()
+                ready.record(s_in)
+            st.wait_event(ready)
+            o, _, _ = layer(x_dev[b], router_w, router_b, local_p)
+            done = torch.cuda.Event()
+            done.record(st)
+            comp_done[b] = done
+            o.record_stream(s_out)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(done)
+                out_host[b].copy_(o, non_blocking=True)
+
+        for i in range(args.warmup):
+            e2e_step(i)
+        torch.cuda.synchronize()
         barrier(world)
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(st)
-        x_dev.copy_(x_host, non_blocking=True)
-        o, _, _ = step() if graph is not None else layer(x_dev, router_w, router_b, local_p)
-        out_host.copy_(o, non_blocking=True)
-        b.record(st)
-        b.synchronize()
-        if i >= args.warmup:
-            e2e.append(a.elapsed_time(b))
-    e2e_ms = max_over_ranks(statistics.mean(e2e), world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for i in range(args.steps):
+            e2e_step(i, e0 if i == 0 else None)
+        e1.record(s_out)
+        torch.cuda.synchronize()
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    else:
+        out_host = torch.empty_like(x_host).pin_memory()
+        x_dev = torch.empty_like(x)
+        e2e = []
+        for i in range(args.warmup + args.steps):
+            barrier(world)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(st)
+            x_dev.copy_(x_host, non_blocking=True)
+            o, _, _ = layer(x_dev, router_w, router_b, local_p)
+            out_host.copy_(o, non_blocking=True)
+            b.record(st)
+            b.synchronize()
+            if i >= args.warmup:
+                e2e.append(a.elapsed_time(b))
+        e2e_ms = max_over_ranks(statistics.mean(e2e), world)
     stats = layer.last_stats
     peaks, peak_src = load_peaks()
     if exchange is not None:
