@@ -275,3 +275,41 @@ def test_experts_and_mlp_backward_match_fp32_autograd():
     r_mdx = omoe.rel_l2(xm.grad.reshape(64, -1).cpu()[keep], xr.grad[keep])
     print(f"mlp: out {r_mo:.2e} dx {r_mdx:.2e}")
     assert r_mo <= 5e-3 and r_mdx <= 1e-2
+
+
+def test_reference_disk_shards_stream_the_b200_mlp(tmp_path):
+    """The reference's on-disk shard format (block_streamer/shards.py:
+    convert_modules writes one flat file per block plus manifest.json) and its
+    DiskBufferPool (StreamedModel(manifest=...)) feed B200GptOssMLP blocks
+    built on ``meta``: the output equals the same blocks resident on the GPU."""
+    import sys
+    import types
+
+    ref_dir = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref")
+    if not os.path.exists(os.path.join(ref_dir, "streamer.py")):
+        pytest.skip("reference package not installed under baseline/_ref")
+    if ref_dir not in sys.path:
+        sys.path.insert(0, ref_dir)
+    from streamer import StreamedModel
+    from block_streamer.shards import convert_modules
+    from blockstreamer_b200 import B200GptOssMLP
+
+    shape = LayerShape(512, 512, 16, 4)
+    cfg = types.SimpleNamespace(hidden_size=shape.hidden, intermediate_size=shape.intermediate,
+                                num_local_experts=shape.experts, num_experts_per_tok=shape.top_k,
+                                swiglu_limit=7.0)
+    states = [make_layer(shape, 30 + layer) for layer in range(3)]
+    manifest = convert_modules(((i, st) for i, st in enumerate(states)), tmp_path)
+    h = make_tokens(96, shape.hidden, 30).to(DEV).reshape(3, 32, shape.hidden)
+    x = h.clone()
+    for st in states:
+        b = B200GptOssMLP(cfg)
+        b.load_state_dict({n: t.to(DEV) for n, t in st.items()}, strict=True, assign=True)
+        h, scores_direct = b(h)
+    model = StreamedModel([B200GptOssMLP(cfg) for _ in states], device=DEV, prefetch_ahead=1, dtype=None,
+                          manifest=manifest)
+    out, scores = model(x)
+    torch.cuda.synchronize()
+    assert torch.equal(out, h)
+    assert torch.equal(scores, scores_direct)
+    model.close()
