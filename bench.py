@@ -37,6 +37,10 @@ METRIC = "MoE-layer tokens/s at gpt-oss-120b shape"
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 FP4_DENSE_NOMINAL_TFLOPS = 9000.0
 L2_BYTES = 126 * 1024 * 1024
+# DRAM bytes per launch (read + write) from one ncu capture of the default
+# workload (profiles/traffic_tc_grouped_gptoss120b_prefill_8192.md)
+NCU_TRAFFIC = {("gptoss120b-prefill-8192", "gate_up"): 1501327360,
+               ("gptoss120b-prefill-8192", "down"): 924871936}
 
 
 def parse_workload(name: str):
@@ -444,7 +448,7 @@ def run_ours(args, rank, world, local):
         achieved = stage_flops[dom] / dur_s / 1e12
         peak = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
         roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                "frac": achieved / peak, "traffic": None, "kernel": dom,
+                "frac": achieved / peak, "traffic": NCU_TRAFFIC.get((args.workload, dom)), "kernel": dom,
                 "peak_source": f"{peak_src} bf16 dense sustained (cuBLAS) — the MMA runs bf16 x bf16"}
     else:
         achieved = stage_bytes[dom] / dur_s / 1e9
