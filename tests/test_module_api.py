@@ -2,6 +2,7 @@
 ``MXFP4Experts`` (block_streamer/gptoss.py:115-128) and transformers' router
 (modeling_gpt_oss.py:117-124), so StreamedModel binds state unchanged."""
 
+import os
 import types
 
 import pytest
@@ -41,7 +42,8 @@ def test_experts_match_reference_module_when_importable():
     """Cross-check against the reference class itself (skipped where it is absent)."""
     try:
         import sys
-        sys.path.insert(0, "/root/reference")
+        from conftest import REPO
+        sys.path.insert(0, os.path.join(REPO, "baseline", "_ref"))   # the installed reference package
         from block_streamer.gptoss import MXFP4Experts
     except Exception:
         pytest.skip("reference not importable here")
