@@ -14,8 +14,8 @@ Submodules:
   ``build``            in-tree build of the library
 """
 
-from .gptoss import (B200GptOssMLP, B200MXFP4Experts, dequantize_expert, install_b200_experts,
-                     install_b200_mlp, mxfp4_matmul)
+from .gptoss import (B200GptOssMLP, B200GptOssMoEBlock, B200MXFP4Experts, dequantize_expert,
+                     install_b200_experts, install_b200_mlp, mxfp4_matmul)
 
-__all__ = ["B200GptOssMLP", "B200MXFP4Experts", "dequantize_expert", "install_b200_experts",
-           "install_b200_mlp", "mxfp4_matmul"]
+__all__ = ["B200GptOssMLP", "B200GptOssMoEBlock", "B200MXFP4Experts", "dequantize_expert",
+           "install_b200_experts", "install_b200_mlp", "mxfp4_matmul"]

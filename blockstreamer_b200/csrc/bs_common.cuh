@@ -175,6 +175,15 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// bf16(residual + bf16(v)) for two packed values: the decoder layer's
+// `residual + mlp(...)` (modeling_gpt_oss.py, GptOssDecoderLayer.forward), where
+// the MLP output is itself a bf16 tensor.
+__device__ __forceinline__ uint32_t add_residual_bf16x2(uint32_t res, float v_lo, float v_hi) {
+  const float lo = __bfloat162float(__float2bfloat16_rn(v_lo)) + bf16lo(res);
+  const float hi = __bfloat162float(__float2bfloat16_rn(v_hi)) + bf16hi(res);
+  return pack_bf16x2(lo, hi);
+}
+
 // SwiGLU of the reference (block_streamer/gptoss.py:130-135) in fp32.
 __device__ __forceinline__ float swiglu(float gate, float up, float alpha, float limit) {
   gate = fminf(gate, limit);

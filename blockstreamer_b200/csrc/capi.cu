@@ -13,8 +13,11 @@ int dispatch_launch(const void* indices, int index_dtype, int64_t T, int64_t k, 
                     const void* x, int64_t H, int32_t* offsets, int32_t* row_of_slot,
                     int32_t* token_of_row, void* x_perm, void* ws, size_t ws_bytes,
                     cudaStream_t st);
+int rmsnorm_launch(const void* x, int64_t T, int64_t H, const void* weight, int w_dtype, float eps, void* out,
+                   cudaStream_t st);
 int combine_launch(const void* y, const int32_t* row_of_slot, const float* weights, int64_t T,
-                   int64_t k, int64_t H, void* out, cudaStream_t st);
+                   int64_t k, int64_t H, void* out, cudaStream_t st,
+                   const void* residual = nullptr);
 int gemv_gate_up_launch(const void* x, const int32_t* offsets, int64_t rows_total, int64_t E,
                         int64_t H, int64_t I, const void* blocks, const void* scales,
                         const void* bias, int bias_f32, float alpha, float limit, void* h,
@@ -35,7 +38,8 @@ int decode_forward(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, in
                    const void* rw, const void* rb, int rdt, float* scores, int32_t* indices,
                    const void* gu_b, const void* gu_s, const void* gu_bias, const void* dn_b,
                    const void* dn_s, const void* dn_bias, int bias_f32, float alpha, float limit,
-                   void* out, void* ws, cudaStream_t st);
+                   void* out, void* ws, cudaStream_t st,
+                   const void* residual = nullptr);
 
 namespace {
 
@@ -187,15 +191,17 @@ extern "C" size_t bs_moe_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_
   return bs::moe_workspace_bytes(T, H, I, E, k);
 }
 
-extern "C" int bs_moe_forward(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, int64_t k,
-                              const void* router_weight, const void* router_bias, int router_dtype,
-                              float* scores, int32_t* indices, const void* gate_up_blocks,
-                              const void* gate_up_scales, const void* gate_up_bias,
-                              const void* down_blocks, const void* down_scales,
-                              const void* down_bias, int bias_dtype, float alpha, float limit,
-                              void* out, void* workspace, size_t workspace_bytes, int algo,
-                              void* stream) {
-  using namespace bs;
+namespace bs {
+namespace {
+// The layer; with residual != NULL the combine also adds it (bf16 + bf16).
+int moe_forward_impl(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, int64_t k,
+                     const void* router_weight, const void* router_bias, int router_dtype,
+                     float* scores, int32_t* indices, const void* gate_up_blocks,
+                     const void* gate_up_scales, const void* gate_up_bias,
+                     const void* down_blocks, const void* down_scales,
+                     const void* down_bias, int bias_dtype, float alpha, float limit,
+                     void* out, void* workspace, size_t workspace_bytes, int algo,
+                     void* stream, const void* residual) {
   BS_ARG(x && scores && indices && out, "bs_moe_forward: null pointer");
   BS_ARG(T >= 0 && H > 0 && I > 0 && E > 0 && k > 0 && k <= E, "bs_moe_forward: bad sizes");
   BS_ARG((router_weight == nullptr) == (router_bias == nullptr),
@@ -223,7 +229,7 @@ extern "C" int bs_moe_forward(const void* x, int64_t T, int64_t H, int64_t I, in
     BS_TRY(check_device());
     return decode_forward(x, T, H, I, E, k, router_weight, router_bias, router_dtype, scores, indices,
                           gate_up_blocks, gate_up_scales, gate_up_bias, down_blocks, down_scales,
-                          down_bias, bias_dtype == BS_F32, alpha, limit, out, workspace, st);
+                          down_bias, bias_dtype == BS_F32, alpha, limit, out, workspace, st, residual);
   }
   const Workspace w = carve(workspace, T, H, I, E, k);
   BS_REQUIRE(workspace_bytes >= w.total, BS_ERR_CAPACITY,
@@ -239,6 +245,50 @@ extern "C" int bs_moe_forward(const void* x, int64_t T, int64_t H, int64_t I, in
                  bias_dtype, alpha, limit, w.h, algo, st));
   BS_TRY(down(w.h, w.offsets, S, S, E, H, I, down_blocks, down_scales, down_bias, bias_dtype, w.y,
               algo, st));
-  BS_TRY(combine_launch(w.y, w.row_of_slot, scores, T, k, H, out, st));
+  BS_TRY(combine_launch(w.y, w.row_of_slot, scores, T, k, H, out, st, residual));
   return BS_OK;
+}
+}  // namespace
+}  // namespace bs
+
+extern "C" int bs_moe_forward(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, int64_t k,
+                              const void* router_weight, const void* router_bias, int router_dtype,
+                              float* scores, int32_t* indices, const void* gate_up_blocks,
+                              const void* gate_up_scales, const void* gate_up_bias,
+                              const void* down_blocks, const void* down_scales,
+                              const void* down_bias, int bias_dtype, float alpha, float limit,
+                              void* out, void* workspace, size_t workspace_bytes, int algo,
+                              void* stream) {
+  return bs::moe_forward_impl(x, T, H, I, E, k, router_weight, router_bias, router_dtype, scores, indices,
+                              gate_up_blocks, gate_up_scales, gate_up_bias, down_blocks, down_scales, down_bias,
+                              bias_dtype, alpha, limit, out, workspace, workspace_bytes, algo, stream, nullptr);
+}
+
+extern "C" size_t bs_moe_block_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t k) {
+  return bs::align_up(bs_moe_workspace_bytes(T, H, I, E, k), 256) + bs::align_up((size_t)T * H * 2, 256);
+}
+
+extern "C" int bs_moe_block_forward(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, int64_t k,
+                                    const void* norm_weight, int norm_dtype, float eps,
+                                    const void* router_weight, const void* router_bias, int router_dtype,
+                                    float* scores, int32_t* indices, const void* gate_up_blocks,
+                                    const void* gate_up_scales, const void* gate_up_bias,
+                                    const void* down_blocks, const void* down_scales, const void* down_bias,
+                                    int bias_dtype, float alpha, float limit, void* out, void* workspace,
+                                    size_t workspace_bytes, int algo, void* stream) {
+  using namespace bs;
+  BS_ARG(x && norm_weight && out && workspace, "bs_moe_block_forward: null pointer");
+  BS_ARG(out != x, "bs_moe_block_forward: out must not alias x (x is the residual)");
+  BS_ARG(T >= 0 && H > 0, "bs_moe_block_forward: bad sizes");
+  if (T == 0) return BS_OK;
+  const size_t layer_ws = align_up(bs_moe_workspace_bytes(T, H, I, E, k), 256);
+  BS_REQUIRE(workspace_bytes >= bs_moe_block_workspace_bytes(T, H, I, E, k), BS_ERR_CAPACITY,
+             "bs_moe_block_forward: workspace of %zu bytes is smaller than the %zu needed", workspace_bytes,
+             bs_moe_block_workspace_bytes(T, H, I, E, k));
+  void* xn = static_cast<char*>(workspace) + layer_ws;
+  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  BS_TRY(rmsnorm_launch(x, T, H, norm_weight, norm_dtype, eps, xn, st));
+  return moe_forward_impl(xn, T, H, I, E, k, router_weight, router_bias, router_dtype, scores, indices,
+                          gate_up_blocks, gate_up_scales, gate_up_bias, down_blocks, down_scales, down_bias,
+                          bias_dtype, alpha, limit, out, workspace, layer_ws, algo, stream, x);
 }

@@ -874,6 +874,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
 __global__ void __launch_bounds__(256) decode_combine_kernel(const float4* __restrict__ y,
                                                              const int* __restrict__ row_of_slot,
                                                              int T, int k, int vecs,
+                                                             const uint2* __restrict__ residual,
                                                              uint2* __restrict__ out) {
   pdl_wait();
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < T * vecs; i += gridDim.x * blockDim.x) {
@@ -888,7 +889,12 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(const float4* __res
       a2 += q.z;
       a3 += q.w;
     }
-    out[i] = make_uint2(pack_bf16x2(a0, a1), pack_bf16x2(a2, a3));
+    if (residual) {
+      const uint2 q = residual[i];
+      out[i] = make_uint2(add_residual_bf16x2(q.x, a0, a1), add_residual_bf16x2(q.y, a2, a3));
+    } else {
+      out[i] = make_uint2(pack_bf16x2(a0, a1), pack_bf16x2(a2, a3));
+    }
   }
 }
 
@@ -1013,7 +1019,7 @@ int decode_forward(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, in
                    const void* rw, const void* rb, int rdt, float* scores, int32_t* indices,
                    const void* gu_b, const void* gu_s, const void* gu_bias, const void* dn_b,
                    const void* dn_s, const void* dn_bias, int bias_f32, float alpha, float limit,
-                   void* out, void* ws, cudaStream_t st) {
+                   void* out, void* ws, cudaStream_t st, const void* residual) {
   BS_ARG(decode_supported(T, H, I, E, k),
          "decode path: need 1 <= T <= %d, E <= 1024, k <= 32, H and I multiples of 64", kMaxDecodeT);
   BS_REQUIRE(((uintptr_t)gu_b | (uintptr_t)dn_b | (uintptr_t)gu_s | (uintptr_t)dn_s) % 16 == 0,
@@ -1088,7 +1094,8 @@ int decode_forward(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, in
   const int vecs = (int)(H / 4);
   const int cgrid = (int)std::max<int64_t>(1, std::min<int64_t>(cdiv(T * vecs, (int64_t)256), sm_count() * 4));
   BS_TRY(launch_pdl(decode_combine_kernel, dim3(cgrid), dim3(256), 0, st, (const float4*)w.y,
-                    (const int*)w.row_of_slot, (int)T, (int)k, vecs, static_cast<uint2*>(out)));
+                    (const int*)w.row_of_slot, (int)T, (int)k, vecs, static_cast<const uint2*>(residual),
+                    static_cast<uint2*>(out)));
   return BS_OK;
 }
 

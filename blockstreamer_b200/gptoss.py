@@ -208,6 +208,47 @@ class B200GptOssMLP(nn.Module):
         return out.reshape(B, S, H).to(hidden_states.dtype), scores.to(self.router.weight.dtype)
 
 
+class _RMSNorm(nn.Module):
+    """Holds ``weight`` [H] under GptOssRMSNorm's name; eps as its ``variance_epsilon``."""
+
+    def __init__(self, hidden: int, eps: float, dtype: torch.dtype) -> None:
+        super().__init__()
+        self.weight = nn.Parameter(torch.empty(hidden, dtype=dtype, device="meta"))
+        self.variance_epsilon = eps
+
+
+class B200GptOssMoEBlock(nn.Module):
+    """The MoE half of transformers' ``GptOssDecoderLayer`` fused around the layer:
+    ``forward(hidden [B,S,H]) -> hidden + mlp(post_attention_layernorm(hidden))``
+    (GptOssDecoderLayer.forward's "Fully Connected" part, modeling_gpt_oss.py),
+    with the decoder layer's parameter names (``post_attention_layernorm.weight``,
+    ``mlp.router.*``, ``mlp.experts.*``).  On the GPU path the norm is one kernel
+    and the residual add happens in the layer's final combine."""
+
+    def __init__(self, config, dtype: torch.dtype = torch.bfloat16, router_dtype: torch.dtype = torch.float32,
+                 norm_dtype: torch.dtype = torch.float32, algo: int = kernels.ALGO_AUTO) -> None:
+        super().__init__()
+        self.post_attention_layernorm = _RMSNorm(config.hidden_size, getattr(config, "rms_norm_eps", 1e-5),
+                                                 norm_dtype)
+        self.mlp = B200GptOssMLP(config, dtype, router_dtype, algo)
+
+    def forward(self, hidden_states: Tensor) -> Tensor:
+        B, S, H = hidden_states.shape
+        norm, mlp, ex = self.post_attention_layernorm, self.mlp, self.mlp.experts
+        if torch.is_grad_enabled() and hidden_states.requires_grad:
+            v = hidden_states.to(torch.float32)
+            v = v * torch.rsqrt(v.pow(2).mean(-1, keepdim=True) + norm.variance_epsilon)
+            normed = (norm.weight * v).to(hidden_states.dtype)
+            out, _ = mlp(normed)
+            return hidden_states + out
+        out, _, _ = kernels.moe_block_forward(
+            hidden_states.reshape(-1, H).to(torch.bfloat16), norm.weight, norm.variance_epsilon,
+            ex.gate_up_proj_blocks, ex.gate_up_proj_scales, ex.gate_up_proj_bias, ex.down_proj_blocks,
+            ex.down_proj_scales, ex.down_proj_bias, mlp.top_k, mlp.router.weight, mlp.router.bias,
+            alpha=ex.alpha, limit=ex.limit, algo=ex.algo)
+        return out.reshape(B, S, H).to(hidden_states.dtype)
+
+
 def install_b200_experts(model: nn.Module, config, dtype=torch.bfloat16) -> int:
     """Swap every ``GptOssExperts`` / ``MXFP4Experts`` for ``B200MXFP4Experts``
     (the counterpart of gptoss.py:180-189)."""

@@ -202,6 +202,20 @@ def moe_down(h, expert_offsets, blocks, scales, bias, algo=ALGO_AUTO, max_rows_p
     return y
 
 
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """GptOssRMSNorm: bf16(weight * (x * rsqrt(mean(x^2) + eps))) per row (bs_rmsnorm)."""
+    _cuda("rmsnorm", x, weight)
+    if x.dtype != torch.bfloat16 or weight.dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("rmsnorm: x must be bf16 and weight bf16 or f32")
+    x = _contig("x", x)
+    T, H = x.shape
+    out = out if out is not None else torch.empty_like(x)
+    with torch.cuda.device(x.device):
+        _lib.call("bs_rmsnorm", _p(x), T, H, _p(_contig("weight", weight)), _DT[weight.dtype], float(eps),
+                  _p(out), _stream(x))
+    return out
+
+
 def combine(y: torch.Tensor, row_of_slot: torch.Tensor, weights: torch.Tensor, num_tokens: int,
             out: torch.Tensor | None = None) -> torch.Tensor:
     """out[t] = sum_s weights[t,s] * y[row_of_slot[t*k+s]] (fp32 sum, bf16 out)."""
@@ -261,6 +275,36 @@ def mxfp4_matmul(x: torch.Tensor, blocks: torch.Tensor, scales: torch.Tensor,
         _lib.call("bs_mxfp4_matmul", _p(x), m, K, _p(_contig("blocks", blocks)),
                   _p(_contig("scales", scales)), N, _p(bias), _p(out), algo, _stream(x))
     return out
+
+
+def moe_block_forward(x: torch.Tensor, norm_weight: torch.Tensor, eps: float, gate_up_blocks,
+                      gate_up_scales, gate_up_bias, down_blocks, down_scales, down_bias, top_k: int,
+                      router_weight, router_bias, alpha=ALPHA, limit=LIMIT, algo=ALGO_AUTO):
+    """x + MoE(RMSNorm(x)) through bs_moe_block_forward: returns (out, scores f32, indices int32)."""
+    _cuda("moe_block_forward", x, norm_weight, gate_up_blocks, gate_up_scales, down_blocks, down_scales,
+          router_weight)
+    if x.dtype != torch.bfloat16:
+        raise ValueError("moe_block_forward: hidden states must be bf16")
+    x = _contig("x", x)
+    T, H = x.shape
+    E, two_i = gate_up_blocks.shape[:2]
+    I = two_i // 2
+    dev = x.device
+    idx = torch.empty(T, top_k, dtype=torch.int32, device=dev)
+    sc = torch.empty(T, top_k, dtype=torch.float32, device=dev)
+    lib = _lib.load()
+    ws = torch.empty(max(lib.bs_moe_block_workspace_bytes(T, H, I, E, top_k), 16), dtype=torch.uint8, device=dev)
+    out = torch.empty_like(x)
+    bias_code = _bias_code(gate_up_bias)
+    if down_bias is not None and down_bias.dtype != gate_up_bias.dtype:
+        down_bias = down_bias.to(gate_up_bias.dtype)
+    with torch.cuda.device(dev):
+        _lib.call("bs_moe_block_forward", _p(x), T, H, I, E, top_k, _p(_contig("norm_weight", norm_weight)),
+                  _DT[norm_weight.dtype], float(eps), _p(router_weight), _p(router_bias),
+                  _DT[router_weight.dtype], _p(sc), _p(idx), _p(gate_up_blocks), _p(gate_up_scales),
+                  _p(gate_up_bias), _p(down_blocks), _p(down_scales), _p(down_bias), bias_code, float(alpha),
+                  float(limit), _p(out), _p(ws), ws.numel(), algo, _stream(x))
+    return out, sc, idx
 
 
 def moe_forward(x: torch.Tensor, gate_up_blocks, gate_up_scales, gate_up_bias, down_blocks,

@@ -238,6 +238,32 @@ int bs_moe_forward(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, in
                    int bias_dtype, float alpha, float limit, void* out, void* workspace,
                    size_t workspace_bytes, int algo, void* stream);
 
+/* RMSNorm of the gpt-oss decoder layer.  Replaces transformers
+ * models/gpt_oss/modeling_gpt_oss.py GptOssRMSNorm.forward:
+ *   out = bf16(weight * (float(x) * rsqrt(mean(float(x)^2) + eps)))
+ * x, out [T, H] bf16 (H a multiple of 8, 16-byte aligned); weight [H] bf16 or
+ * f32 (w_dtype). */
+int bs_rmsnorm(const void* x, int64_t T, int64_t H, const void* weight, int w_dtype, float eps,
+               void* out, void* stream);
+
+/* The MoE half of a gpt-oss decoder layer, fused around the layer: replaces
+ * GptOssDecoderLayer.forward's "Fully Connected" part (modeling_gpt_oss.py):
+ *   out = x + mlp(post_attention_layernorm(x))
+ * = bs_rmsnorm into the workspace, then bs_moe_forward on the normalized rows,
+ * whose final combine also adds the residual x (bf16 + bf16, as the reference
+ * adds two bf16 tensors).  Same arguments as bs_moe_forward plus the norm
+ * weight [H] (norm_dtype bf16 or f32) and eps; out must not alias x.
+ * Workspace: bs_moe_block_workspace_bytes(T, H, I, E, k). */
+size_t bs_moe_block_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t k);
+int bs_moe_block_forward(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, int64_t k,
+                         const void* norm_weight, int norm_dtype, float eps,
+                         const void* router_weight, const void* router_bias, int router_dtype,
+                         float* scores, int32_t* indices,
+                         const void* gate_up_blocks, const void* gate_up_scales, const void* gate_up_bias,
+                         const void* down_blocks, const void* down_scales, const void* down_bias,
+                         int bias_dtype, float alpha, float limit, void* out, void* workspace,
+                         size_t workspace_bytes, int algo, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -313,3 +313,43 @@ def test_reference_disk_shards_stream_the_b200_mlp(tmp_path):
     assert torch.equal(out, h)
     assert torch.equal(scores, scores_direct)
     model.close()
+
+
+@pytest.mark.parametrize("algo", [kernels.ALGO_AUTO, kernels.ALGO_TCGEN05, kernels.ALGO_GEMV])
+def test_moe_block_norm_and_residual_vs_reference_math(algo):
+    """B200GptOssMoEBlock = x + mlp(post_attention_layernorm(x)) (the MoE half of
+    GptOssDecoderLayer.forward): RMSNorm kernel against GptOssRMSNorm's torch
+    math (within one bf16 ulp), and the block against the fp32 reference math
+    on the normalized rows plus the residual (rel-L2 <= 5e-3, routing exact
+    away from near-ties)."""
+    import types
+    from blockstreamer_b200 import B200GptOssMoEBlock
+
+    shape = CASES["tiny"]
+    T = 64
+    cfg = types.SimpleNamespace(hidden_size=shape.hidden, intermediate_size=shape.intermediate,
+                                num_local_experts=shape.experts, num_experts_per_tok=shape.top_k,
+                                swiglu_limit=7.0, rms_norm_eps=1e-5)
+    p = make_layer(shape, 6)
+    g = torch.Generator().manual_seed(6)
+    nw = (1.0 + 0.1 * torch.randn(shape.hidden, generator=g)).float()
+    x = make_tokens(T, shape.hidden, 6)
+    # GptOssRMSNorm.forward's math
+    v = x.float()
+    xn = (nw * (v * torch.rsqrt(v.pow(2).mean(-1, keepdim=True) + 1e-5))).to(torch.bfloat16)
+    got_n = kernels.rmsnorm(x.to(DEV), nw.to(DEV), 1e-5).cpu()
+    ulp = (xn.float().abs() * 2.0 ** -7).clamp_min(1e-30)
+    assert bool(((got_n.float() - xn.float()).abs() <= ulp).all())
+
+    blk = B200GptOssMoEBlock(cfg, algo=algo)
+    state = {"post_attention_layernorm.weight": nw}
+    state.update({"mlp." + n: t for n, t in p.items()})
+    blk.load_state_dict({n: t.to(DEV) for n, t in state.items()}, strict=True, assign=True)
+    out = blk(x.to(DEV).reshape(1, T, -1)).reshape(T, -1).cpu()
+    lg, s_ref, i_ref = omoe.router(xn.float(), p["router.weight"], p["router.bias"], shape.top_k)
+    ref = x.float() + omoe.experts_fp32(xn, i_ref, s_ref, experts_of(p))
+    keep = ~omoe.near_tie_tokens(omoe.router_logits_f64(xn, p["router.weight"], p["router.bias"]),
+                                 shape.top_k, 1e-6 + omoe.ROUTER_LOGIT_ERR, lg)
+    rel = omoe.rel_l2(out.float()[keep], ref[keep])
+    print(f"algo {algo}: block rel_l2 {rel:.2e} ({int(keep.sum())} of {T} tokens)")
+    assert rel <= 5e-3
