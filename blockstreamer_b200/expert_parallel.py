@@ -149,6 +149,12 @@ class P2PExchange:
                       self.E, self.me, self.cap, self.src_rows,
                       torch.cuda.current_stream(self.device).cuda_stream)
 
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
     def close(self):
         """Collective: unmap the peers, then free this rank's buffer."""
         if self._closed:
