@@ -109,3 +109,24 @@ def test_expert_parallel_exchange_layout():
     base = ctypes.c_void_p(16)
     st = lib.bs_ep_p2p_dispatch(base, 2880, base, base, base, base, 3, 128, 0, 3, 1, base, None)
     assert st == _lib.BS_ERR_INVALID_ARGUMENT or st == _lib.BS_ERR_UNSUPPORTED   # 128 experts over 3 ranks
+
+
+def test_norm_and_block_entry_points_reject_bad_arguments():
+    """bs_rmsnorm / bs_moe_block_forward check pointers, sizes, dtypes, aliasing
+    and workspace capacity before any device work."""
+    lib = _lib.load()
+    p = ctypes.c_void_p(0x1000)
+    q = ctypes.c_void_p(0x2000)
+    assert lib.bs_rmsnorm(None, 4, 64, p, _lib.BS_F32, 1e-5, p, None) == _lib.BS_ERR_INVALID_ARGUMENT
+    assert lib.bs_rmsnorm(p, 4, 60, p, _lib.BS_F32, 1e-5, q, None) == _lib.BS_ERR_INVALID_ARGUMENT  # H % 8
+    assert lib.bs_rmsnorm(p, 4, 64, p, _lib.BS_I32, 1e-5, q, None) == _lib.BS_ERR_INVALID_ARGUMENT  # dtype
+    assert lib.bs_rmsnorm(ctypes.c_void_p(0x1008), 4, 64, p, _lib.BS_F32, 1e-5, q, None) == _lib.BS_ERR_MISALIGNED
+    args = [4, 64, 64, 8, 2, p, _lib.BS_F32, 1e-5, p, p, _lib.BS_F32, p, p, p, p, p, p, p, p, _lib.BS_BF16,
+            1.702, 7.0]
+    # out aliasing x (x is the residual)
+    assert lib.bs_moe_block_forward(p, *args, p, q, 1 << 30, 0, None) == _lib.BS_ERR_INVALID_ARGUMENT
+    assert "alias" in _err(lib)
+    # workspace too small
+    need = lib.bs_moe_block_workspace_bytes(4, 64, 64, 8, 2)
+    assert need > lib.bs_moe_workspace_bytes(4, 64, 64, 8, 2)
+    assert lib.bs_moe_block_forward(p, *args, q, q, need - 1, 0, None) == _lib.BS_ERR_CAPACITY
