@@ -56,6 +56,8 @@ SIGNATURES = {
     "bs_combine": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp, _vp]),
     "bs_mxfp4_matmul": (_i32, [_vp, _i64, _i64, _vp, _vp, _i64, _vp, _vp, _i32, _vp]),
     "bs_moe_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64]),
+    "bs_moe_decode": (_i32, [_vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _i32, _vp, _vp,
+                             _vp, _vp, _vp, _vp, _vp, _vp, _i32, _f32, _f32, _vp, _vp, _sz, _vp]),
     "bs_rmsnorm": (_i32, [_vp, _i64, _i64, _vp, _i32, _f32, _vp, _vp]),
     "bs_moe_block_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64]),
     "bs_moe_block_forward": (_i32, [_vp, _i64, _i64, _i64, _i64, _i64, _vp, _i32, _f32, _vp, _vp, _i32, _vp,

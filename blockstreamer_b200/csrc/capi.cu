@@ -264,6 +264,19 @@ extern "C" int bs_moe_forward(const void* x, int64_t T, int64_t H, int64_t I, in
                               bias_dtype, alpha, limit, out, workspace, workspace_bytes, algo, stream, nullptr);
 }
 
+extern "C" int bs_moe_decode(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, int64_t k,
+                             const void* router_weight, const void* router_bias, int router_dtype,
+                             float* scores, int32_t* indices, const void* gate_up_blocks,
+                             const void* gate_up_scales, const void* gate_up_bias,
+                             const void* down_blocks, const void* down_scales, const void* down_bias,
+                             int bias_dtype, float alpha, float limit, void* out, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+  return bs::moe_forward_impl(x, T, H, I, E, k, router_weight, router_bias, router_dtype, scores, indices,
+                              gate_up_blocks, gate_up_scales, gate_up_bias, down_blocks, down_scales, down_bias,
+                              bias_dtype, alpha, limit, out, workspace, workspace_bytes, BS_ALGO_MX, stream,
+                              nullptr);
+}
+
 extern "C" size_t bs_moe_block_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t k) {
   return bs::align_up(bs_moe_workspace_bytes(T, H, I, E, k), 256) + bs::align_up((size_t)T * H * 2, 256);
 }

@@ -238,6 +238,21 @@ int bs_moe_forward(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, in
                    int bias_dtype, float alpha, float limit, void* out, void* workspace,
                    size_t workspace_bytes, int algo, void* stream);
 
+/* Decode-shape layer: bs_moe_forward with BS_ALGO_MX (T <= 64 tokens; H and I
+ * multiples of 64; blocks and scales 16-byte aligned): router, top-k and
+ * dispatch, gate_up + SwiGLU and down on tcgen05 block-scaled MMAs over the
+ * stored e2m1 codes, combine -- four launches chained with programmatic
+ * dependent launch.  Replaces the same reference lines as bs_moe_forward
+ * (modeling_gpt_oss.py:140-146 with gptoss.py:137-177) at decode sizes.
+ * Workspace: bs_moe_workspace_bytes. */
+int bs_moe_decode(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, int64_t k,
+                  const void* router_weight, const void* router_bias, int router_dtype,
+                  float* scores, int32_t* indices,
+                  const void* gate_up_blocks, const void* gate_up_scales, const void* gate_up_bias,
+                  const void* down_blocks, const void* down_scales, const void* down_bias,
+                  int bias_dtype, float alpha, float limit, void* out, void* workspace,
+                  size_t workspace_bytes, void* stream);
+
 /* RMSNorm of the gpt-oss decoder layer.  Replaces transformers
  * models/gpt_oss/modeling_gpt_oss.py GptOssRMSNorm.forward:
  *   out = bf16(weight * (float(x) * rsqrt(mean(float(x)^2) + eps)))

@@ -157,3 +157,37 @@ def test_decode_matches_across_calls_and_graph():
     torch.cuda.synchronize()
     assert torch.equal(a, c)
     assert kernels.device_status(clear=True) == 0
+
+
+def test_bs_moe_decode_entry_point_matches_forward():
+    """bs_moe_decode (the decode-shape C entry point) gives the same bits as
+    bs_moe_forward with BS_ALGO_MX, and rejects more than 64 tokens."""
+    import ctypes
+    from blockstreamer_b200 import _lib
+    shape = LayerShape(512, 512, 32, 4)
+    p = make_layer(shape, 12, device=DEV)
+    pe = [p[n] for n in ("experts.gate_up_proj_blocks", "experts.gate_up_proj_scales",
+                         "experts.gate_up_proj_bias", "experts.down_proj_blocks",
+                         "experts.down_proj_scales", "experts.down_proj_bias")]
+    vp = lambda t: ctypes.c_void_p(t.data_ptr())
+    lib = _lib.load()
+    for T in (1, 8):
+        x = make_tokens(T, shape.hidden, 12, device=DEV)
+        ref, sc_ref, idx_ref = kernels.moe_forward(x, *pe, shape.top_k, router_weight=p["router.weight"],
+                                                   router_bias=p["router.bias"], algo=kernels.ALGO_MX)
+        ws = torch.empty(lib.bs_moe_workspace_bytes(T, shape.hidden, shape.intermediate, shape.experts,
+                                                    shape.top_k), dtype=torch.uint8, device=DEV)
+        out = torch.empty_like(x)
+        sc = torch.empty(T, shape.top_k, dtype=torch.float32, device=DEV)
+        idx = torch.empty(T, shape.top_k, dtype=torch.int32, device=DEV)
+        _lib.call("bs_moe_decode", vp(x), T, shape.hidden, shape.intermediate, shape.experts, shape.top_k,
+                  vp(p["router.weight"]), vp(p["router.bias"]), _lib.BS_F32, vp(sc), vp(idx),
+                  *[vp(t) for t in pe], _lib.BS_BF16, 1.702, 7.0, vp(out), vp(ws), ws.numel(),
+                  ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        torch.cuda.synchronize()
+        assert torch.equal(out, ref) and torch.equal(idx, idx_ref) and torch.equal(sc, sc_ref)
+    big = torch.empty(65, shape.hidden, dtype=torch.bfloat16, device=DEV)
+    with pytest.raises(ValueError):
+        _lib.call("bs_moe_decode", vp(big), 65, shape.hidden, shape.intermediate, shape.experts, shape.top_k,
+                  None, None, _lib.BS_F32, vp(sc), vp(idx), *[vp(t) for t in pe], _lib.BS_BF16, 1.702, 7.0,
+                  vp(big), vp(ws), ws.numel(), None)
