@@ -3,22 +3,29 @@
 Default workload: the gpt-oss-120b-shaped MoE layer (H = I = 2880, 128 experts,
 top-4, MXFP4 experts) over an 8192-token prefill batch, all experts resident
 on each GPU at N=1.  A "step" is one layer forward: router, dispatch, gate_up +
-SwiGLU, down, weighted combine.  Inputs are seeded synthetic tensors (no
-checkpoint exists offline); the weights (1.69 GB) are larger than L2, so no
-extra L2 flush is needed between steps.
+SwiGLU, down, weighted combine, replayed from a CUDA graph (at every N).
+Inputs are seeded synthetic tensors (no checkpoint exists offline); the
+weights (1.69 GB) are larger than L2, so no extra L2 flush is needed between
+steps.  The default run also measures BASELINE configs 2 and 3 (20b prefill of
+4096 tokens; 120b decode of 1, 8 and 64 tokens) and reports them under
+"configs", each with its own roofline.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                   [--workload gptoss120b-prefill-8192|gptoss120b-decode-T|gptoss20b-prefill-4096|
                               gptoss120b-zipf-16384-streamed]
 
-``--impl reference`` times the reference's CPU path restated in ``oracle``
-(bf16 per-expert loop, the CPU baseline) on a bounded sample on rank 0.
+``--impl reference`` runs the reference's own CPU path -- transformers'
+GptOssTopKRouter and block_streamer.gptoss.MXFP4Experts from the installed
+package under baseline/_ref -- on rank 0: every step routes all tokens and
+runs one group of the hit experts, so that the steps together run the whole
+layer once (or a whole number of times); the line says what ran.
 """
 
 from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import statistics
 import sys
@@ -34,13 +41,19 @@ from blockstreamer_b200.synthetic import (CASES, algorithmic_bytes, algorithmic_
                                           expert_bytes, make_layer, make_tokens)
 
 METRIC = "MoE-layer tokens/s at gpt-oss-120b shape"
+DEFAULT_WORKLOAD = "gptoss120b-prefill-8192"
+EXTRA_WORKLOADS = ("gptoss20b-prefill-4096", "gptoss120b-decode-1", "gptoss120b-decode-8",
+                   "gptoss120b-decode-64")
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 FP4_DENSE_NOMINAL_TFLOPS = 9000.0
 L2_BYTES = 126 * 1024 * 1024
-# DRAM bytes per launch (read + write) from one ncu capture of the default
-# workload (profiles/traffic_tc_grouped_gptoss120b_prefill_8192.md)
+# DRAM bytes per launch (read + write) of the expert GEMMs, from one earlier
+# ncu capture of the default workload; stored constants, not measured per run.
 NCU_TRAFFIC = {("gptoss120b-prefill-8192", "gate_up"): 1501327360,
                ("gptoss120b-prefill-8192", "down"): 924871936}
+# a timed region shorter than this runs at the burst clock: its tensor-bound
+# kernels are compared with the burst (not the sustained) GEMM peak
+SUSTAINED_REGION_S = 1.0
 
 
 def parse_workload(name: str):
@@ -62,6 +75,13 @@ def load_peaks():
             d = json.load(f)
         return d, "measured"
     return PEAKS_FALLBACK, "fallback"
+
+
+def tensor_peak(peaks, region_s):
+    """(peak TFLOP/s, label): burst for a short timed region, sustained for a long one."""
+    if region_s >= SUSTAINED_REGION_S and "bf16_tflops_sustained" in peaks:
+        return peaks["bf16_tflops_sustained"], "bf16 dense sustained (cuBLAS, seconds-long loop)"
+    return peaks["bf16_tflops"], f"bf16 dense burst (cuBLAS; timed region {region_s * 1e3:.0f} ms)"
 
 
 class ClockSampler:
@@ -169,10 +189,12 @@ def cpu_inputs(key: str, case_id: int, T: int):
     return shape, make_layer(shape, case_id), make_tokens(T, shape.hidden, case_id)
 
 
-def cpu_sample(shape, p, x, experts_in_sample: int = 1):
-    """Time the reference's CPU path (oracle port) on a bounded sample of the
-    workload: the router over all T tokens plus the full expert work of
-    ``experts_in_sample`` experts; the expert time is scaled to all hit experts."""
+def cpu_sample(shape, p, x, experts_in_sample: int = 8):
+    """The cpu_baseline of our arm: the oracle port (the reference's bf16
+    per-expert loop restated on torch CPU ops) on a bounded sample of the
+    workload -- the router over all T tokens plus the full expert work of
+    ``experts_in_sample`` of the hit experts; the expert time is scaled to
+    all hit experts, as the sample string says."""
     from oracle import moe as omoe
     T = x.shape[0]
     threads = os.cpu_count() or 1
@@ -186,33 +208,118 @@ def cpu_sample(shape, p, x, experts_in_sample: int = 1):
     t0 = time.perf_counter()
     omoe.experts_port(x, idx, sc, pe, experts_subset=subset)
     t_exp = time.perf_counter() - t0
-    t_total = t_router + t_exp * len(hit) / max(len(subset), 1)
+    scale = len(hit) / max(len(subset), 1)
+    t_total = t_router + t_exp * scale
     return {"value": T / t_total, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": (f"router over all {T} tokens ({t_router:.2f} s) + the full bf16 expert loop "
-                       f"of {len(subset)} of {len(hit)} hit experts ({t_exp:.2f} s), expert time "
-                       f"scaled x{len(hit) / max(len(subset), 1):.0f}"),
+            "sample": (f"oracle port: router over all {T} tokens ({t_router:.2f} s) + the bf16 expert "
+                       f"loop of {len(subset)} of {len(hit)} hit experts ({t_exp:.2f} s); expert time "
+                       f"scaled by {scale:.1f} to all hit experts"),
             "seconds": t_router + t_exp}
 
 
+def load_reference():
+    """The reference's own modules from its installed package (baseline/_ref):
+    (MXFP4Experts, GptOssConfig, GptOssTopKRouter), or (None, reason)."""
+    ref_dir = os.path.join(REPO, "baseline", "_ref")
+    if not os.path.exists(os.path.join(ref_dir, "block_streamer", "gptoss.py")):
+        return None, "the reference package is not installed under baseline/_ref"
+    if ref_dir not in sys.path:
+        sys.path.insert(0, ref_dir)
+    try:
+        from block_streamer.gptoss import MXFP4Experts
+        from transformers.models.gpt_oss.configuration_gpt_oss import GptOssConfig
+        from transformers.models.gpt_oss.modeling_gpt_oss import GptOssTopKRouter
+    except Exception as e:  # noqa: BLE001 - reported in the line
+        return None, f"importing the reference failed: {type(e).__name__}: {e}"
+    return (MXFP4Experts, GptOssConfig, GptOssTopKRouter), None
+
+
 def run_reference(args, rank, world):
+    """The reference arm: transformers' GptOssTopKRouter + the reference's
+    MXFP4Experts (block_streamer/gptoss.py:137-177), unmodified, on the host
+    cores.  The whole layer takes tens of seconds on a CPU, so its hit experts
+    are split into groups: every step routes all T tokens and runs one group
+    (its experts' (token, slot) rows through MXFP4Experts.forward, exactly the
+    per-expert work of the full layer), and the steps cycle over the groups a
+    whole number of times.  layer time = mean router time + the sum over the
+    groups of their mean expert time; value = T / layer time."""
     key, case_id, T = parse_workload(args.workload)
     if rank != 0:
         return
-    vals = []
-    cb = None
+    mods, why = load_reference()
+    if mods is None:
+        print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
+        return
+    MXFP4Experts, GptOssConfig, GptOssTopKRouter = mods
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
     shape, p, x = cpu_inputs(key, case_id, T)
-    for i in range(args.warmup + args.steps):
-        r = cpu_sample(shape, p, x, experts_in_sample=1)
-        if i >= args.warmup:
-            vals.append(r["value"])
-            cb = r
-    v = statistics.median(vals)
-    cb["value"] = v
+    E, k = shape.experts, shape.top_k
+    cfg = GptOssConfig(hidden_size=shape.hidden, intermediate_size=shape.intermediate, num_local_experts=E,
+                       num_experts_per_tok=k, swiglu_limit=shape.swiglu_limit)
+    router = GptOssTopKRouter(cfg)
+    router.weight.data = p["router.weight"]
+    router.bias.data = p["router.bias"]
+    names = ("gate_up_proj_blocks", "gate_up_proj_scales", "gate_up_proj_bias",
+             "down_proj_blocks", "down_proj_scales", "down_proj_bias")
+
+    def group_module(e0, e1):
+        gcfg = GptOssConfig(hidden_size=shape.hidden, intermediate_size=shape.intermediate,
+                            num_local_experts=e1 - e0, num_experts_per_tok=1,
+                            swiglu_limit=shape.swiglu_limit)
+        m = MXFP4Experts(gcfg, torch.bfloat16)
+        for n in names:
+            setattr(m, n, torch.nn.Parameter(p["experts." + n][e0:e1], requires_grad=False))
+        return m
+
+    with torch.no_grad():
+        _, sc, idx = router(x.float())
+    hit = sorted(set(idx.reshape(-1).tolist()))
+    per = max(1, math.ceil(len(hit) / max(args.steps, 1)))
+    groups = [hit[i:i + per] for i in range(0, len(hit), per)]
+    cycles = max(1, args.steps // len(groups))
+
+    def run_group(g):
+        # the rows of the group's experts, one per (token, slot), with the
+        # experts renumbered into the group module (its experts are a
+        # contiguous slice of the layer's; experts of the range that no
+        # token picked cost nothing in MXFP4Experts.forward)
+        e0, e1 = g[0], g[-1] + 1
+        sel = (idx >= e0) & (idx < e1)
+        tok, slot = torch.nonzero(sel, as_tuple=True)
+        m = group_module(e0, e1)
+        t0 = time.perf_counter()
+        with torch.no_grad():
+            router(x.float())
+            t1 = time.perf_counter()
+            m(x[tok], (idx[tok, slot] - e0).unsqueeze(1), sc[tok, slot].unsqueeze(1))
+        t2 = time.perf_counter()
+        return t1 - t0, t2 - t1
+
+    for i in range(args.warmup):          # warm-up: one expert each, untimed
+        run_group(hit[i % len(hit): i % len(hit) + 1])
+    t_router, t_group = [], [[] for _ in groups]
+    wall0 = time.perf_counter()
+    for _ in range(cycles):
+        for gi, g in enumerate(groups):
+            tr, te = run_group(g)
+            t_router.append(tr)
+            t_group[gi].append(te)
+    wall = time.perf_counter() - wall0
+    steps = cycles * len(groups)
+    layer_s = statistics.mean(t_router) + sum(statistics.mean(v) for v in t_group)
+    v = T / layer_s
+    sample = (f"reference GptOssTopKRouter + block_streamer.gptoss.MXFP4Experts (baseline/_ref) on "
+              f"{threads} host threads: {steps} steps, each routing all {T} tokens and running a group of "
+              f"{per} of the {len(hit)} hit experts ({len(groups)} groups, {cycles} full cycle(s) = the "
+              f"whole layer {cycles} time(s)); layer time {layer_s:.2f} s = router {statistics.mean(t_router):.3f} s "
+              f"+ the groups' expert times; {wall:.1f} s of timed CPU work")
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * T / v,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic", "config": {"workload": args.workload},
-            "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "steps": steps, "warmup": args.warmup, "ms_per_step": 1e3 * wall / steps,
+            "layer_ms": 1e3 * layer_s, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic", "config": {"workload": args.workload, "tokens": T},
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": "reference",
+                             "sample": sample},
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -221,6 +328,8 @@ def run_reference(args, rank, world):
 
 STAGES = ("router", "dispatch", "gate_up", "down", "combine")
 LAUNCHES = {"router": 3, "dispatch": 4, "gate_up": 1, "down": 1, "combine": 1}  # router: 2 at T <= 64
+ALGOS = {"auto": kernels.ALGO_AUTO, "gemv": kernels.ALGO_GEMV, "tcgen05": kernels.ALGO_TCGEN05,
+         "mx": kernels.ALGO_MX}
 
 
 def layer_stages(x, p, k, algo, bufs):
@@ -267,189 +376,216 @@ def layer_stages(x, p, k, algo, bufs):
     def combine():
         kernels.combine(bufs["y"], bufs["d"].row_of_slot, bufs["sc"], T, out=bufs["out"])
 
-    return {"router": router, "dispatch": dispatch, "gate_up": gate_up, "down": down, "combine": combine}
+    return [("router", router), ("dispatch", dispatch), ("gate_up", gate_up), ("down", down),
+            ("combine", combine)]
 
 
-def run_ours(args, rank, world, local):
-    key, case_id, T_total = parse_workload(args.workload)
+def capture(fn):
+    """fn's launches as a CUDA graph (fn has run eagerly before, so every
+    one-time set-up is done)."""
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    return g
+
+
+def graphed_stage_ms(stages, steps, world):
+    """Per-stage device time: each stage captured in a CUDA graph of its own,
+    the graphs replayed in layer order, with events between replays on the
+    launch stream (mean over ``steps`` layers; max over ranks)."""
+    for _, fn in stages:
+        fn()
+    torch.cuda.synchronize()
+    graphs = [(name, capture(fn)) for name, fn in stages]
+    for _, g in graphs:
+        g.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    st = torch.cuda.current_stream()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(len(graphs) + 1)] for _ in range(steps)]
+    for i in range(steps):
+        evs[i][0].record(st)
+        for j, (_, g) in enumerate(graphs):
+            g.replay()
+            evs[i][j + 1].record(st)
+    torch.cuda.synchronize()
+    out = {name: max_over_ranks(statistics.mean(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(steps)),
+                                world)
+           for j, (name, _) in enumerate(graphs)}
+    del graphs
+    return out
+
+
+def time_steps(step, steps, flush_buf, world):
+    """Device time of one step (ms): K steps between two events, or, with an
+    L2 flush buffer, each step after a 2xL2 write, timed on its own."""
+    st = torch.cuda.current_stream()
+    barrier(world)
+    torch.cuda.synchronize()
+    if flush_buf is not None:
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(steps)]
+        for a, b in evs:
+            flush_buf.fill_(1)
+            a.record(st)
+            step()
+            b.record(st)
+        torch.cuda.synchronize()
+        ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    else:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(steps):
+            step()
+        e1.record(st)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+    barrier(world)
+    return max_over_ranks(ms, world)
+
+
+def e2e_ms(layer_call, x, steps, warmup, world, pipelined):
+    """The layer through the public API with host buffers: every step copies
+    its tokens in from pinned host memory and its output back out.
+    Pipelined (prefill sizes): the copies run on their own streams, so step
+    i+1's host->device copy and step i-1's device->host copy overlap step i's
+    layer (double-buffered, as a serving loop runs it); timed from the first
+    timed step's input copy to the last timed step's output copy.  Otherwise
+    (decode sizes, kilobyte copies): copy in, layer, copy out per step."""
+    st = torch.cuda.current_stream()
+    x_host = x.cpu().pin_memory()
+    out_host = [torch.empty_like(x_host).pin_memory() for _ in range(2)]
+    x_dev = [torch.empty_like(x) for _ in range(2)]
+    if pipelined:
+        s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
+        comp_done = [None, None]
+
+        def e2e_step(i, first_event=None):
+            b = i % 2
+            with torch.cuda.stream(s_in):
+                if comp_done[b] is not None:
+                    s_in.wait_event(comp_done[b])   # the layer two steps back has read x_dev[b]
+                if first_event is not None:
+                    first_event.record(s_in)
+                x_dev[b].copy_(x_host, non_blocking=True)
+                ready = torch.cuda.Event()
+                ready.record(s_in)
+            st.wait_event(ready)
+            o = layer_call(x_dev[b])
+            done = torch.cuda.Event()
+            done.record(st)
+            comp_done[b] = done
+            o.record_stream(s_out)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(done)
+                out_host[b].copy_(o, non_blocking=True)
+
+        for i in range(warmup):
+            e2e_step(i)
+        torch.cuda.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for i in range(steps):
+            e2e_step(i, e0 if i == 0 else None)
+        e1.record(s_out)
+        torch.cuda.synchronize()
+        return max_over_ranks(e0.elapsed_time(e1) / steps, world)
+    times = []
+    for i in range(warmup + steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        x_dev[0].copy_(x_host, non_blocking=True)
+        o = layer_call(x_dev[0])
+        out_host[0].copy_(o, non_blocking=True)
+        b.record(st)
+        b.synchronize()
+        if i >= warmup:
+            times.append(a.elapsed_time(b))
+    return max_over_ranks(statistics.mean(times), world)
+
+
+def measure(workload, args, world, local):
+    """One workload on one GPU: value (graph-replayed layer, device-timed),
+    per-stage times, e2e through the public API, and the rooflines."""
+    key, case_id, T = parse_workload(workload)
     shape = CASES[key]
+    k, E, H, I = shape.top_k, shape.experts, shape.hidden, shape.intermediate
     dev = torch.device("cuda", torch.cuda.current_device())
-    if case_id == 5:
-        return run_bench_streamed(args, rank, world, shape, case_id, T_total)
-    if world > 1:
-        return run_bench_ep(args, rank, world, local, shape, case_id, T_total)
-    T = T_total
-    k = shape.top_k
-    algo = {"auto": kernels.ALGO_AUTO, "gemv": kernels.ALGO_GEMV, "tcgen05": kernels.ALGO_TCGEN05,
-            "mx": kernels.ALGO_MX}[args.algo]
+    algo = ALGOS[args.algo]
     # the decode path: one bs_moe_forward call = 4 launches (route, gate_up, down, combine)
     mx_path = algo == kernels.ALGO_MX or (algo == kernels.ALGO_AUTO and T <= 64)
     p = make_layer(shape, case_id, device=dev)
-    x = make_tokens(T, shape.hidden, case_id, device=dev)
-    E = shape.experts
+    x = make_tokens(T, H, case_id, device=dev)
     gu = (p["experts.gate_up_proj_blocks"], p["experts.gate_up_proj_scales"], p["experts.gate_up_proj_bias"])
     dn = (p["experts.down_proj_blocks"], p["experts.down_proj_scales"], p["experts.down_proj_bias"])
-    ws = torch.empty(kernels._lib.load().bs_moe_workspace_bytes(T, shape.hidden, shape.intermediate, E, k),
-                     dtype=torch.uint8, device=dev)
+    ws = torch.empty(kernels._lib.load().bs_moe_workspace_bytes(T, H, I, E, k), dtype=torch.uint8, device=dev)
 
-    def eager_step():
-        return kernels.moe_forward(x, *gu, *dn, k, router_weight=p["router.weight"],
-                                   router_bias=p["router.bias"], algo=algo, workspace=ws)
+    def layer(xin, workspace=ws):
+        return kernels.moe_forward(xin, *gu, *dn, k, router_weight=p["router.weight"],
+                                   router_bias=p["router.bias"], algo=algo, workspace=workspace)
 
     for _ in range(args.warmup):
-        out, sc, idx = eager_step()
+        out, sc, idx = layer(x)
     torch.cuda.synchronize()
-    step = eager_step
-    graphed = T <= 64 and not args.no_graph
+    step = lambda: layer(x)  # noqa: E731
+    graphed = not args.no_graph
+    graph_ok = None
     if graphed:
-        # decode shapes are launch-bound: replay the whole layer from a CUDA graph
+        # the whole layer (no host synchronization inside) replayed from a CUDA graph
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
-            g_out = eager_step()
-
-        def step():
-            graph.replay()
-            return g_out
-        step()
+            g_out, _, _ = layer(x)
+        graph.replay()
         torch.cuda.synchronize()
+        graph_ok = bool(torch.equal(g_out, out))
+        step = graph.replay
     distinct = int(torch.unique(idx).numel())
     counts = torch.bincount(idx.reshape(-1).long(), minlength=E)
     assert kernels.device_status(clear=True) == 0
 
-    # --- value: K layer forwards, device-timed.  When the step's touched expert
-    # weights would fit in L2 (decode shapes), L2 is flushed before every step
-    # and each step is timed by its own event pair.
-    st = torch.cuda.current_stream()
     flush_l2 = distinct * expert_bytes(shape) < 2 * L2_BYTES
     flush_buf = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev) if flush_l2 else None
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
-        barrier(world)
-        torch.cuda.synchronize()
-        if flush_l2:
-            evs_v = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                     for _ in range(args.steps)]
-            for a, b in evs_v:
-                flush_buf.fill_(1)
-                a.record(st)
-                step()
-                b.record(st)
-            torch.cuda.synchronize()
-            ms_local = statistics.mean(a.elapsed_time(b) for a, b in evs_v)
-        else:
-            ev0.record(st)
-            for _ in range(args.steps):
-                step()
-            ev1.record(st)
-            torch.cuda.synchronize()
-            ms_local = ev0.elapsed_time(ev1) / args.steps
-        barrier(world)
-    ms = max_over_ranks(ms_local, world)
+        ms = time_steps(step, args.steps, flush_buf, world)
     value = T / (ms * 1e-3)
+    del flush_buf
 
-    # --- per-stage breakdown over K more steps (same kernels, events between stages).
-    # The decode path's four launches sit inside one C call; its breakdown comes
+    # per-stage breakdown: each C-ABI stage from its own graph replay.  The
+    # decode path's four launches sit inside one C call; its breakdown comes
     # from the ncu launch list instead.
     if mx_path:
         stage_ms = {"layer": ms}
     else:
         bufs = {}
-        stages = layer_stages(x, p, k, algo, bufs)
-        for fn in stages.values():
-            fn()
-        torch.cuda.synchronize()
-        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(len(STAGES) + 1)] for _ in range(args.steps)]
-        for i in range(args.steps):
-            evs[i][0].record(st)
-            for j, name in enumerate(STAGES):
-                stages[name]()
-                evs[i][j + 1].record(st)
-        torch.cuda.synchronize()
-        stage_ms = {n: statistics.mean(evs[i][j].elapsed_time(evs[i][j + 1]) for i in range(args.steps))
-                    for j, n in enumerate(STAGES)}
+        stage_ms = graphed_stage_ms(layer_stages(x, p, k, algo, bufs), args.steps, world)
+        del bufs
 
-    # --- e2e through the public API with host buffers.  Every step copies its
-    # tokens in from pinned host memory and its output back out; the copies
-    # run on their own streams, so step i+1's host->device copy and step
-    # i-1's device->host copy overlap step i's layer (double-buffered inputs
-    # and outputs, as a serving loop would run it).  Timed from the first
-    # timed step's input copy to the last timed step's output copy.
-    x_host = x.cpu().pin_memory()
-    out_host = [torch.empty_like(x_host).pin_memory() for _ in range(2)]
-    x_dev = [torch.empty_like(x) for _ in range(2)]
-    s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
-    comp_done = [None, None]
-
-    def e2e_step(i, first_event=None):
-        b = i % 2
-        with torch.cuda.stream(s_in):
-            if comp_done[b] is not None:
-                s_in.wait_event(comp_done[b])   # the layer two steps back has read x_dev[b]
-            if first_event is not None:
-                first_event.record(s_in)
-            x_dev[b].copy_(x_host, non_blocking=True)
-            ready = torch.cuda.Event()
-            ready.record(s_in)
-        st.wait_event(ready)
-        o, _, _ = kernels.moe_forward(x_dev[b], *gu, *dn, k, router_weight=p["router.weight"],
-                                      router_bias=p["router.bias"], algo=algo)
-        done = torch.cuda.Event()
-        done.record(st)
-        comp_done[b] = done
-        o.record_stream(s_out)
-        with torch.cuda.stream(s_out):
-            s_out.wait_event(done)
-            out_host[b].copy_(o, non_blocking=True)
-
-    pipelined = T > 64   # decode sizes: kilobyte copies, the cross-stream events would dominate
-    if pipelined:
-        for i in range(args.warmup):
-            e2e_step(i)
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        for i in range(args.steps):
-            e2e_step(i, e0 if i == 0 else None)
-        e1.record(s_out)
-        torch.cuda.synchronize()
-        e2e_ms_v = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
-    else:
-        e2e_ms = []
-        for i in range(args.warmup + args.steps):
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(st)
-            x_dev[0].copy_(x_host, non_blocking=True)
-            o, _, _ = kernels.moe_forward(x_dev[0], *gu, *dn, k, router_weight=p["router.weight"],
-                                          router_bias=p["router.bias"], algo=algo, workspace=ws)
-            out_host[0].copy_(o, non_blocking=True)
-            b.record(st)
-            b.synchronize()
-            if i >= args.warmup:
-                e2e_ms.append(a.elapsed_time(b))
-        e2e_ms_v = max_over_ranks(statistics.mean(e2e_ms), world)
+    pipelined = T > 64
+    ms_e2e = e2e_ms(lambda xin: layer(xin, None)[0], x, args.steps, args.warmup, world, pipelined)
 
     # --- roofline of the dominant kernel
     peaks, peak_src = load_peaks()
-    flops_pair = 6.0 * shape.hidden * shape.intermediate
     S = T * k
-    stage_flops = {"gate_up": S * 4.0 * shape.hidden * shape.intermediate,
-                   "down": S * 2.0 * shape.hidden * shape.intermediate,
-                   "router": 2.0 * T * shape.hidden * E}
-    G = shape.hidden // 32
-    gu_bytes = distinct * (2 * shape.intermediate * G * 17 + 2 * shape.intermediate * 2) + S * shape.hidden * 2 + S * shape.intermediate * 2
-    dn_bytes = distinct * (shape.hidden * (shape.intermediate // 32) * 17 + shape.hidden * 2) + S * shape.intermediate * 2 + S * shape.hidden * 2
-    stage_bytes = {"gate_up": gu_bytes, "down": dn_bytes,
-                   "router": E * shape.hidden * 4 + T * shape.hidden * 2,
-                   "dispatch": 2 * S * shape.hidden * 2, "combine": S * shape.hidden * 2 + T * shape.hidden * 2,
+    stage_flops = {"gate_up": S * 4.0 * H * I, "down": S * 2.0 * H * I, "router": 2.0 * T * H * E}
+    G = H // 32
+    gu_bytes = distinct * (2 * I * G * 17 + 2 * I * 2) + S * H * 2 + S * I * 2
+    dn_bytes = distinct * (H * (I // 32) * 17 + H * 2) + S * I * 2 + S * H * 2
+    stage_bytes = {"gate_up": gu_bytes, "down": dn_bytes, "router": E * H * 4 + T * H * 2,
+                   "dispatch": 2 * S * H * 2, "combine": S * H * 2 + T * H * 2,
                    "layer": algorithmic_bytes(T, shape, distinct)}
     dom = max(stage_ms, key=stage_ms.get)
     tensor_bound = (S / max(distinct, 1)) > 64 and dom in ("gate_up", "down")
     dur_s = stage_ms[dom] * 1e-3
+    region_s = ms * args.steps * 1e-3
     if tensor_bound:
         achieved = stage_flops[dom] / dur_s / 1e12
-        peak = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
+        peak, plabel = tensor_peak(peaks, region_s)
+        traffic = NCU_TRAFFIC.get((workload, dom))
         roof = {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                "frac": achieved / peak, "traffic": NCU_TRAFFIC.get((args.workload, dom)), "kernel": dom,
-                "peak_source": f"{peak_src} bf16 dense sustained (cuBLAS) — the MMA runs bf16 x bf16"}
+                "frac": achieved / peak, "traffic": traffic, "kernel": dom,
+                "peak_source": f"{peak_src} {plabel}; the MMA runs bf16 x bf16",
+                "traffic_source": ("stored constant from one ncu capture of this workload (DRAM read + write "
+                                   "per launch), not measured in this run") if traffic else None}
     else:
         achieved = stage_bytes[dom] / dur_s / 1e9
         peak = peaks["hbm_gbs"]
@@ -460,8 +596,7 @@ def run_ours(args, rank, world, local):
             roof["kernel"] = ("whole layer (route, gate_up, down, combine launches): weights of the "
                               "touched experts + router weights + tokens over the device-timed step; "
                               "a lower bound for the expert kernels, which move >97% of the bytes")
-    roof["algorithmic"] = {"flops": stage_flops.get(dom), "bytes": stage_bytes.get(dom),
-                           "launch_ms": stage_ms[dom]}
+    roof["algorithmic"] = {"flops": stage_flops.get(dom), "bytes": stage_bytes.get(dom), "launch_ms": stage_ms[dom]}
     layer_flops = algorithmic_flops(T, shape)
     layer_bytes = algorithmic_bytes(T, shape, distinct)
     t_fp4 = layer_flops / (FP4_DENSE_NOMINAL_TFLOPS * 1e12)
@@ -469,32 +604,54 @@ def run_ours(args, rank, world, local):
     layer_roof = {"flops": layer_flops, "bytes": layer_bytes, "distinct_experts": distinct,
                   "floor_us_fp4_nominal": t_fp4 * 1e6, "floor_us_hbm_measured": t_hbm * 1e6,
                   "frac_of_fp4_hbm_roofline": max(t_fp4, t_hbm) / (ms * 1e-3),
-                  "frac_of_bf16_measured": (layer_flops / (ms * 1e-3) / 1e12) / peaks["bf16_tflops"],
-                  "stage_ms": stage_ms}
-
-    clocks = clk.summary()
-    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+                  "frac_of_bf16_burst_measured": (layer_flops / (ms * 1e-3) / 1e12) / peaks["bf16_tflops"],
+                  "stage_ms": stage_ms,
+                  "stage_ms_source": ("each C-ABI stage replayed from its own CUDA graph, events between "
+                                      "replays" if not mx_path else "whole layer (one C call)")}
+    return {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": args.workload, "tokens": T, "hidden": shape.hidden,
-                       "intermediate": shape.intermediate, "experts": E, "top_k": k,
-                       "weights": "MXFP4 e2m1 + e8m0 scales (uniform codes, scales U{%d..%d})" % (shape.scale_lo, shape.scale_hi),
-                       "algo": args.algo, "cuda_graph": graphed,
+            "config": {"workload": workload, "tokens": T, "hidden": H, "intermediate": I, "experts": E,
+                       "top_k": k,
+                       "weights": "MXFP4 e2m1 + e8m0 scales (uniform codes, scales U{%d..%d})" % (
+                           shape.scale_lo, shape.scale_hi),
+                       "algo": args.algo, "cuda_graph": graphed, "graph_output_equals_eager": graph_ok,
                        "l2": ("L2 flushed (256 MB write) before each timed step; steps timed individually"
                               if flush_l2 else "inputs larger than L2 (expert weights read per step exceed L2)"),
                        "expert_rows_min_max": [int(counts.min()), int(counts.max())]},
             "roofline": roof, "layer_roofline": layer_roof,
-            "e2e": {"value": T / (e2e_ms_v * 1e-3), "unit": "tokens/s",
+            "e2e": {"value": T / (ms_e2e * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": x.numel() * 2,
                     "api": "blockstreamer_b200.kernels.moe_forward -> bs_moe_forward",
                     "pipelining": ("copies on their own streams: step i+1's H2D and step i-1's D2H "
                                    "overlap step i's layer (double-buffered)") if pipelined else
                                   "none (decode size: copy, layer, copy back per step)"},
-            "clocks": clocks,
+            "clocks": clk.summary(),
             "gpu_launches": (4 if mx_path else sum(LAUNCHES.values())) * args.steps}
+
+
+def run_ours(args, rank, world, local):
+    key, case_id, T_total = parse_workload(args.workload)
+    shape = CASES[key]
+    if case_id == 5:
+        return run_bench_streamed(args, rank, world, shape, case_id, T_total)
+    if world > 1:
+        return run_bench_ep(args, rank, world, local, shape, case_id, T_total)
+    line = measure(args.workload, args, world, local)
+    torch.cuda.empty_cache()
+    if args.workload == DEFAULT_WORKLOAD and not args.no_extra:
+        # BASELINE configs 2 and 3 in the same run, each with its own roofline
+        extra = {}
+        for w in EXTRA_WORKLOADS:
+            r = measure(w, args, world, local)
+            torch.cuda.empty_cache()
+            extra[w] = {n: r[n] for n in ("value", "unit", "ms_per_step", "roofline", "layer_roofline", "e2e",
+                                          "clocks", "gpu_launches")}
+            extra[w]["config"] = r["config"]
+        line["configs"] = extra
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        shape_c, p_c, x_c = cpu_inputs(key, case_id, T)
-        cb = cpu_sample(shape_c, p_c, x_c, experts_in_sample=1)
+        shape_c, p_c, x_c = cpu_inputs(key, case_id, T_total)
+        cb = cpu_sample(shape_c, p_c, x_c)
         line["cpu_baseline"] = {k2: cb[k2] for k2 in ("value", "unit", "cores", "kind", "sample")}
     if rank == 0:
         print(json.dumps(line), flush=True)
@@ -504,7 +661,9 @@ def run_ours(args, rank, world, local):
 
 def run_bench_ep(args, rank, world, local, shape, case_id, T_total):
     """The same layer split over `world` ranks: experts [r*E/R, (r+1)*E/R) and
-    T/R tokens per rank (strong scaling: the 8192-token batch is fixed)."""
+    T/R tokens per rank (strong scaling: the 8192-token batch is fixed).
+    After timing, every rank checks its output slice against the single-GPU
+    layer on the same tokens (outside the timed region)."""
     import torch.distributed as dist
     from blockstreamer_b200.expert_parallel import ExpertParallelMoE, P2PExchange, shard_experts
 
@@ -514,9 +673,8 @@ def run_bench_ep(args, rank, world, local, shape, case_id, T_total):
     Tr = T_total // world
     full = make_layer(shape, case_id, device=dev)
     router_w, router_b = full["router.weight"], full["router.bias"]
-    local_p = shard_experts({k.split(".", 1)[1]: v for k, v in full.items() if k.startswith("experts.")},
-                            rank, world)
-    del full
+    full_e = {k.split(".", 1)[1]: v for k, v in full.items() if k.startswith("experts.")}
+    local_p = shard_experts(full_e, rank, world)
     x_all = make_tokens(T_total, shape.hidden, case_id, device=dev)
     x = x_all[rank * Tr:(rank + 1) * Tr].contiguous()
     del x_all
@@ -530,100 +688,66 @@ def run_bench_ep(args, rank, world, local, shape, case_id, T_total):
         return layer(x, router_w, router_b, local_p)
 
     for _ in range(args.warmup):
-        step()
+        out_eager, _, _ = step()
     torch.cuda.synchronize()
     # The peer-memory path has no host synchronization: one layer call is
-    # captured as a CUDA graph (per rank) and replayed; x is its static input.
+    # captured as a CUDA graph (per rank) and replayed, as at N = 1.
     graph = None
+    g_out = None
     if exchange is not None and not args.no_graph:
         graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
-            g_out = step()
+            g_out, _, _ = step()
         torch.cuda.synchronize()
-    eager_step = step
-    if graph is not None:
-        def step():
-            graph.replay()
-            return g_out
-    st = torch.cuda.current_stream()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        barrier(world)
-        torch.cuda.synchronize()
-        ev0.record(st)
-        for _ in range(args.steps):
-            step()
-        ev1.record(st)
-        torch.cuda.synchronize()
-        barrier(world)
-    ms = max_over_ranks(ev0.elapsed_time(ev1) / args.steps, world)
-    value = T_total / (ms * 1e-3)
-    # per-stage breakdown (same steps launched eagerly, events at stage boundaries)
-    stage_ms = {}
-    for _ in range(args.steps):
-        layer.marks = []
-        eager_step()
-        torch.cuda.synchronize()
-        for (_, a), (name, b) in zip(layer.marks[:-1], layer.marks[1:]):
-            stage_ms[name] = stage_ms.get(name, 0.0) + a.elapsed_time(b) / args.steps
-    layer.marks = None
-    # e2e: this rank's tokens in from pinned host memory, its output back out
-    x_host = x.cpu().pin_memory()
-    if exchange is not None:
-        # peer-memory path (no host sync): copies on their own streams,
-        # double-buffered, overlapping the layer as in the single-GPU e2e; the
-        # ranks stay in step through the exchange's device flags
-        out_host = [torch.empty_like(x_host).pin_memory() for _ in range(2)]
-        x_dev = [torch.empty_like(x) for _ in range(2)]
-        s_in, s_out = torch.cuda.Stream(), torch.cuda.Stream()
-        comp_done = [None, None]
-
-        def e2e_step(i, first_event=None):
-            b = i % 2
-            with torch.cuda.stream(s_in):
-                if comp_done[b] is not None:
-                    s_in.wait_event(comp_done[b])
-                if first_event is not None:
-                    first_event.record(s_in)
-                x_dev[b].copy_(x_host, non_blocking=True)
-                ready = torch.cuda.Event()
-                ready.record(s_in)
-            st.wait_event(ready)
-            o, _, _ = layer(x_dev[b], router_w, router_b, local_p)
-            done = torch.cuda.Event()
-            done.record(st)
-            comp_done[b] = done
-            o.record_stream(s_out)
-            with torch.cuda.stream(s_out):
-                s_out.wait_event(done)
-                out_host[b].copy_(o, non_blocking=True)
-
-        for i in range(args.warmup):
-            e2e_step(i)
-        torch.cuda.synchronize()
-        barrier(world)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        for i in range(args.steps):
-            e2e_step(i, e0 if i == 0 else None)
-        e1.record(s_out)
-        torch.cuda.synchronize()
-        e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+        timed = graph.replay
     else:
-        out_host = torch.empty_like(x_host).pin_memory()
-        x_dev = torch.empty_like(x)
-        e2e = []
-        for i in range(args.warmup + args.steps):
-            barrier(world)
-            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            a.record(st)
-            x_dev.copy_(x_host, non_blocking=True)
-            o, _, _ = layer(x_dev, router_w, router_b, local_p)
-            out_host.copy_(o, non_blocking=True)
-            b.record(st)
-            b.synchronize()
-            if i >= args.warmup:
-                e2e.append(a.elapsed_time(b))
-        e2e_ms = max_over_ranks(statistics.mean(e2e), world)
+        timed = step
+    with ClockSampler(local) as clk:
+        ms = time_steps(timed, args.steps, None, world)
+    value = T_total / (ms * 1e-3)
+    result = g_out if g_out is not None else step()[0]
+    torch.cuda.synchronize()
+    result = result.clone()
+
+    # per-stage breakdown: peer-memory path from per-stage graph replays; the
+    # NCCL path (host-synchronizing) from eager events at stage boundaries
+    if exchange is not None:
+        stages, _ = layer.p2p_stages(x, router_w, router_b, local_p)
+        stage_ms = graphed_stage_ms(stages, args.steps, world)
+        stage_src = "each stage replayed from its own CUDA graph, events between replays (max over ranks)"
+    else:
+        stage_ms = {}
+        for _ in range(args.steps):
+            layer.marks = []
+            step()
+            torch.cuda.synchronize()
+            for (_, a), (name, b) in zip(layer.marks[:-1], layer.marks[1:]):
+                stage_ms[name] = stage_ms.get(name, 0.0) + a.elapsed_time(b) / args.steps
+        layer.marks = None
+        stage_src = "eager launches, events at stage boundaries (rank 0)"
+
+    ms_e2e = e2e_ms(lambda xin: layer(xin, router_w, router_b, local_p)[0], x, args.steps, args.warmup, world,
+                    pipelined=exchange is not None)
+
+    # parity: this rank's slice against the single-GPU layer on its tokens
+    ref, _, _ = kernels.moe_forward(x, full_e["gate_up_proj_blocks"], full_e["gate_up_proj_scales"],
+                                    full_e["gate_up_proj_bias"], full_e["down_proj_blocks"],
+                                    full_e["down_proj_scales"], full_e["down_proj_bias"], shape.top_k,
+                                    router_weight=router_w, router_bias=router_b)
+    torch.cuda.synchronize()
+    exact = bool(torch.equal(result, ref))
+    rel = float((result.float() - ref.float()).norm() / ref.float().norm().clamp_min(1e-30))
+    status = kernels.device_status(clear=True)
+    flags = torch.tensor([1.0 if exact else 0.0, rel, float(status)], dtype=torch.float64, device=dev)
+    worst = flags.clone()
+    dist.all_reduce(worst[1:], op=dist.ReduceOp.MAX)
+    dist.all_reduce(worst[:1], op=dist.ReduceOp.MIN)
+    all_exact, worst_rel, worst_status = bool(worst[0] > 0.5), float(worst[1]), int(worst[2])
+    parity_ok = worst_status == 0 and (all_exact or worst_rel <= 5e-3)
+    parity = (("ok: every rank's output bit-identical to the single-GPU layer on its tokens" if all_exact
+               else f"ok: max rel-L2 {worst_rel:.2e} against the single-GPU layer") if parity_ok
+              else f"FAILED: max rel-L2 {worst_rel:.2e}, device status {worst_status}")
+
     stats = layer.last_stats
     peaks, peak_src = load_peaks()
     if exchange is not None:
@@ -638,11 +762,12 @@ def run_bench_ep(args, rank, world, local, shape, case_id, T_total):
     exp_ms = stage_ms.get("experts", 0.0)
     exp_flops = S_local * 6.0 * shape.hidden * shape.intermediate
     achieved = exp_flops / (exp_ms * 1e-3) / 1e12 if exp_ms else 0.0
-    peak = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
+    peak, plabel = tensor_peak(peaks, ms * args.steps * 1e-3)
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "parity": parity,
                 "config": {"workload": args.workload, "tokens": T_total, "tokens_per_rank": Tr,
                            "experts_per_rank": shape.experts // world, "parallelism": f"ep{world}",
                            "collective": collective,
@@ -652,9 +777,9 @@ def run_bench_ep(args, rank, world, local, shape, case_id, T_total):
                 "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                              "frac": achieved / peak if peak else None, "traffic": None,
                              "kernel": "experts (gate_up + down, rank 0)",
-                             "peak_source": f"{peak_src} bf16 dense sustained (cuBLAS)"},
-                "layer_roofline": {"stage_ms_rank0": stage_ms},
-                "e2e": {"value": T_total / (e2e_ms * 1e-3), "unit": "tokens/s",
+                             "peak_source": f"{peak_src} {plabel}"},
+                "layer_roofline": {"stage_ms": stage_ms, "stage_ms_source": stage_src},
+                "e2e": {"value": T_total / (ms_e2e * 1e-3), "unit": "tokens/s",
                         "h2d_bytes_per_step": x.numel() * 2 * world,
                         "d2h_bytes_per_step": x.numel() * 2 * world,
                         "api": "blockstreamer_b200.expert_parallel.ExpertParallelMoE"},
@@ -663,6 +788,8 @@ def run_bench_ep(args, rank, world, local, shape, case_id, T_total):
     del graph
     if exchange is not None:
         exchange.close()
+    if not parity_ok:
+        raise SystemExit(3)
 
 
 # ---------------------------------------------------------------- streamed stack (config 5)
@@ -791,10 +918,12 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", default="gptoss120b-prefill-8192")
-    ap.add_argument("--algo", choices=["auto", "gemv", "tcgen05", "mx"], default="auto")
+    ap.add_argument("--workload", default=DEFAULT_WORKLOAD)
+    ap.add_argument("--algo", choices=sorted(ALGOS), default="auto")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--no-graph", action="store_true", help="decode shapes: launch eagerly")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="default workload: skip measuring configs 2 and 3 in the same run")
+    ap.add_argument("--no-graph", action="store_true", help="launch every step eagerly")
     ap.add_argument("--ep-transport", choices=["p2p", "nccl"], default="p2p",
                     help="N > 1: exchange rows over peer memory (library kernels) or NCCL all-to-all")
     args = ap.parse_args()

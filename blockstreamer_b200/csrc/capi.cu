@@ -1,8 +1,17 @@
 // C-ABI entry points that compose the kernels: expert projections (GEMV or
 // tcgen05 grouped GEMM), mxfp4_matmul, and the whole-layer forward.
+#include <nvtx3/nvToolsExt.h>
+
 #include "bs_common.cuh"
 
 namespace bs {
+
+// NVTX range over one stage's launches (host-side; nsys/ncu show it beside
+// the kernels; costs nothing without a profiler attached).
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+};
 
 int router_launch(const void* x, int x_dtype, const void* weight, const void* bias, int w_dtype,
                   int64_t T, int64_t H, int64_t E, int64_t k, float* logits, float* scores,
@@ -227,6 +236,7 @@ int moe_forward_impl(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, 
                "bs_moe_forward: workspace of %zu bytes is smaller than the %zu needed", workspace_bytes,
                need);
     BS_TRY(check_device());
+    NvtxRange r("bs.decode_layer");
     return decode_forward(x, T, H, I, E, k, router_weight, router_bias, router_dtype, scores, indices,
                           gate_up_blocks, gate_up_scales, gate_up_bias, down_blocks, down_scales,
                           down_bias, bias_dtype == BS_F32, alpha, limit, out, workspace, st, residual);
@@ -235,16 +245,29 @@ int moe_forward_impl(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, 
   BS_REQUIRE(workspace_bytes >= w.total, BS_ERR_CAPACITY,
              "bs_moe_forward: workspace of %zu bytes is smaller than the %zu needed",
              workspace_bytes, w.total);
-  if (router_weight)
+  NvtxRange layer_range("bs.layer");
+  if (router_weight) {
+    NvtxRange r("bs.router");
     BS_TRY(router_launch(x, BS_BF16, router_weight, router_bias, router_dtype, T, H, E, k, nullptr,
                          scores, indices, BS_I32, w.router, w.router_bytes, st));
-  BS_TRY(dispatch_launch(indices, BS_I32, T, k, E, x, H, w.offsets, w.row_of_slot, w.token_of_row,
+  }
+  {
+    NvtxRange r("bs.dispatch");
+    BS_TRY(dispatch_launch(indices, BS_I32, T, k, E, x, H, w.offsets, w.row_of_slot, w.token_of_row,
                          w.x_perm, w.dispatch, w.dispatch_bytes, st));
+  }
   const int64_t S = T * k;
-  BS_TRY(gate_up(w.x_perm, w.offsets, S, S, E, H, I, gate_up_blocks, gate_up_scales, gate_up_bias,
+  {
+    NvtxRange r("bs.gate_up");
+    BS_TRY(gate_up(w.x_perm, w.offsets, S, S, E, H, I, gate_up_blocks, gate_up_scales, gate_up_bias,
                  bias_dtype, alpha, limit, w.h, algo, st));
-  BS_TRY(down(w.h, w.offsets, S, S, E, H, I, down_blocks, down_scales, down_bias, bias_dtype, w.y,
+  }
+  {
+    NvtxRange r("bs.down");
+    BS_TRY(down(w.h, w.offsets, S, S, E, H, I, down_blocks, down_scales, down_bias, bias_dtype, w.y,
               algo, st));
+  }
+  NvtxRange r("bs.combine");
   BS_TRY(combine_launch(w.y, w.row_of_slot, scores, T, k, H, out, st, residual));
   return BS_OK;
 }

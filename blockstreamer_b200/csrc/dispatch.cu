@@ -201,8 +201,15 @@ int launch_dispatch(const IdxT* idx, int64_t T, int64_t k, int64_t E, const void
 
 }  // namespace
 
+// Sizes the dispatch accepts; checked before any size arithmetic, so that
+// nothing below can overflow (nblk * E * 8 <= 2^23 * 1024 * 8 bytes).
+bool dispatch_sizes_ok(int64_t T, int64_t k, int64_t E) {
+  return T >= 0 && k > 0 && k <= 65536 / kTokBlock && E > 0 && E <= 1024 &&
+         T <= ((int64_t)INT32_MAX - 1) / k;
+}
+
 size_t dispatch_workspace_bytes(int64_t T, int64_t k, int64_t E) {
-  (void)k;
+  if (!dispatch_sizes_ok(T, k, E)) return 0;  // rejected by the entry points anyway
   const int64_t nblk = cdiv(std::max<int64_t>(T, 1), kTokBlock);
   return align_up((size_t)(2 * nblk * E) * sizeof(int), 256);
 }
@@ -213,9 +220,9 @@ int dispatch_launch(const void* indices, int index_dtype, int64_t T, int64_t k, 
                     cudaStream_t st) {
   BS_ARG(indices && offsets && row_of_slot && token_of_row, "bs_dispatch: null pointer");
   BS_ARG(index_dtype == BS_I32 || index_dtype == BS_I64, "bs_dispatch: indices must be int32/int64");
-  BS_ARG(T >= 0 && k > 0 && E > 0 && E <= 1024, "bs_dispatch: need 0 < E <= 1024, k > 0");
-  BS_ARG(T * k < (int64_t)INT32_MAX, "bs_dispatch: too many slots");
-  BS_ARG(kTokBlock * k * 1 <= 65536, "bs_dispatch: top_k too large");
+  BS_ARG(dispatch_sizes_ok(T, k, E),
+         "bs_dispatch: need 0 < E <= 1024, 0 < k <= %d and T * k < 2^31 (T=%lld k=%lld E=%lld)",
+         65536 / kTokBlock, (long long)T, (long long)k, (long long)E);
   if (x || x_perm) {
     BS_ARG(x && x_perm && H > 0, "bs_dispatch: x and x_perm go together");
     BS_ARG((H * 2) % 16 == 0, "bs_dispatch: hidden size must be a multiple of 8");
@@ -257,8 +264,7 @@ extern "C" int bs_dispatch(const void* indices, int index_dtype, int64_t T, int6
 // Allocation-free dispatch (bs_dispatch_noalloc).
 //
 // Some callers cannot allocate device memory at the point where they dispatch
-// tokens: code running while a CUDA graph is being captured (cudaMalloc is not
-// permitted inside a capture), serving loops that must not stall on the device
+// tokens: serving loops that must not stall on the device-wide
 // synchronization cudaMalloc/cudaFree imply, runtimes that pre-reserve all
 // device memory in their own pools, and foreign-language callers (ctypes, cgo,
 // JNI) that have no allocator to hand a workspace from.  For them this entry
@@ -279,7 +285,8 @@ void* g_noalloc_ptr[64] = {};
 
 // Device address of the scratch array on the current device.  The array's name
 // is only a host-side handle, so the address is looked up once per device, with
-// that device current, on the first call made on it.
+// that device current, on the first call made on it, and cached for the
+// process (a cudaDeviceReset would make the cached address stale).
 int noalloc_scratch(void** out) {
   int dev = 0;
   BS_CUDA(cudaGetDevice(&dev));
@@ -302,7 +309,9 @@ extern "C" int bs_dispatch_noalloc(const void* indices, int index_dtype, int64_t
                                    int32_t* row_of_slot, int32_t* token_of_row, void* x_perm,
                                    void* stream) {
   using namespace bs;
-  BS_ARG(T >= 0 && k > 0 && E > 0, "bs_dispatch_noalloc: bad sizes");
+  BS_ARG(dispatch_sizes_ok(T, k, E),
+         "bs_dispatch_noalloc: need 0 < E <= 1024, 0 < k <= %d and T * k < 2^31 (T=%lld k=%lld E=%lld)",
+         65536 / kTokBlock, (long long)T, (long long)k, (long long)E);
   const size_t need = dispatch_workspace_bytes(T, k, E);
   BS_REQUIRE(need <= kNoAllocScratchBytes, BS_ERR_CAPACITY,
              "bs_dispatch_noalloc: T=%lld, E=%lld needs %zu bytes of scratch, above the fixed %zu "

@@ -6,8 +6,10 @@
 // no multicast object, no TMA multicast).  Its layout (ep_layout):
 //   flags   [3][kMaxRanks] u32: counts / rows / results from source s arrived
 //           (each holds the epoch of the last layer call that set it), two
-//           local launch counters and this rank's epoch (layer calls so far,
-//           advanced on the device, so a captured CUDA graph replays correctly);
+//           local launch counters, this rank's epoch (layer calls so far,
+//           advanced on the device, so a captured CUDA graph replays correctly)
+//           and this rank's buffer sizes (cap_rows, src_rows), published so
+//           that every peer can bound the stores it makes into this buffer;
 //   counts  [R][E] i32: row s = source s's rows per global expert;
 //   recv    [cap_rows][H] bf16: rows this rank's experts process, expert-major
 //           and, within an expert, source-major (the grouped GEMMs read them
@@ -31,6 +33,12 @@
 //                         flags.results[me] on every rank;
 //   5. ep_arrived_kernel  wait for every destination's results (then the
 //                         combine kernel reads yback).
+// Capacity: a rank whose dispatched rows exceed its src_rows sends nothing
+// (its counts go out as zeros) and records BS_ERR_CAPACITY; a sender skips any
+// row that would land at or beyond its destination's published cap_rows, and a
+// result row beyond its source's published src_rows, recording the same code;
+// a receiver clamps its local offsets to its cap_rows.  So no argument can
+// make a kernel write outside a peer's buffer.
 // Reuse across calls is safe without extra handshakes: a rank starts call n+1
 // only after its combine of call n, which follows every destination's step 4
 // of call n, which follows that destination's GEMMs over recv (stream order).
@@ -48,6 +56,8 @@ constexpr int kMaxExperts = 1024;
 constexpr long long kWaitCycles = 4000000000LL;
 constexpr int kCounts = 0, kRows = 1, kResults = 2;  // flag groups
 constexpr int kCtrScatter = 3 * kMaxRanks, kCtrReturn = 3 * kMaxRanks + 1, kEpoch = 3 * kMaxRanks + 2;
+constexpr int kCapRows = 3 * kMaxRanks + 3, kSrcRows = 3 * kMaxRanks + 4;  // this buffer's sizes
+constexpr int kNumFlags = 3 * kMaxRanks + 5;
 
 struct EPLayout {
   size_t flags, counts, recv, yback, total;
@@ -59,7 +69,7 @@ __host__ __device__ inline EPLayout ep_layout(int64_t R, int64_t E, int64_t H, i
   EPLayout L;
   size_t o = 0;
   L.flags = o;
-  o = al(o + 4 * (3 * kMaxRanks + 3));
+  o = al(o + 4 * kNumFlags);
   L.counts = o;
   o = al(o + (size_t)R * E * 4);
   L.recv = o;
@@ -112,16 +122,25 @@ __device__ __forceinline__ int last_le(const int* a, int n, int v) {
 
 __global__ void __launch_bounds__(256) ep_counts_kernel(const int* __restrict__ offsets,
                                                         const uint64_t* __restrict__ bases, int R, int E,
-                                                        int me, EPLayout L) {
+                                                        int me, EPLayout L, int cap_rows, int src_rows,
+                                                        int* status) {
   __shared__ uint32_t epoch;
+  __shared__ int over;
   if (threadIdx.x == 0) {
-    uint32_t* ep = at<uint32_t>(bases[me], L.flags) + kEpoch;
-    epoch = *ep + 1;
-    *ep = epoch;
+    uint32_t* fl = at<uint32_t>(bases[me], L.flags);
+    epoch = fl[kEpoch] + 1;
+    fl[kEpoch] = epoch;
+    // sizes of this rank's buffer, for the peers' bounds checks (ordered
+    // before the counts flags below by the fence and the release)
+    fl[kCapRows] = (uint32_t)cap_rows;
+    fl[kSrcRows] = (uint32_t)src_rows;
+    over = offsets[E] > src_rows;
+    if (over) record_status(status, BS_ERR_CAPACITY);
   }
+  __syncthreads();
   for (int i = threadIdx.x; i < R * E; i += blockDim.x) {
     const int d = i / E, e = i - d * E;
-    at<int>(bases[d], L.counts)[me * E + e] = offsets[e + 1] - offsets[e];
+    at<int>(bases[d], L.counts)[me * E + e] = over ? 0 : offsets[e + 1] - offsets[e];
   }
   __threadfence_system();
   __syncthreads();
@@ -133,12 +152,13 @@ __global__ void __launch_bounds__(256) ep_scatter_kernel(const uint4* __restrict
                                                          const int* __restrict__ offsets,
                                                          const int* __restrict__ token_of_row,
                                                          const uint64_t* __restrict__ bases, int R, int E,
-                                                         int me, EPLayout L, int* status) {
+                                                         int me, EPLayout L, int src_rows, int* status) {
   extern __shared__ int sm[];
   int* cm = sm;            // [R][E]
   int* pos = cm + R * E;   // [E]: first recv row of this rank's rows of expert e at its destination
   int* off = pos + E;      // [E + 1]: this rank's dispatch offsets
   __shared__ int ok;
+  __shared__ int cap[kMaxRanks];  // every destination's published cap_rows
   const uint64_t mine = bases[me];
   uint32_t* flags = at<uint32_t>(mine, L.flags);
   const uint32_t epoch = *reinterpret_cast<volatile uint32_t*>(flags + kEpoch);
@@ -148,6 +168,9 @@ __global__ void __launch_bounds__(256) ep_scatter_kernel(const uint4* __restrict
   const volatile int* cmg = at<int>(mine, L.counts);
   for (int i = threadIdx.x; i < R * E; i += blockDim.x) cm[i] = cmg[i];
   for (int i = threadIdx.x; i <= E; i += blockDim.x) off[i] = offsets[i];
+  // the destinations published their sizes before raising their counts flags
+  for (int d = threadIdx.x; d < R; d += blockDim.x)
+    cap[d] = (int)*reinterpret_cast<const volatile uint32_t*>(at<uint32_t>(bases[d], L.flags) + kCapRows);
   __syncthreads();
   const int El = E / R;
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
@@ -160,11 +183,17 @@ __global__ void __launch_bounds__(256) ep_scatter_kernel(const uint4* __restrict
   }
   __syncthreads();
   const int lane = threadIdx.x & 31;
-  const int rows = off[E];
+  // more rows than the exchange was sized for: ep_counts_kernel sent zero
+  // counts and recorded the error; send nothing (the flags below still rise)
+  const int rows = off[E] > src_rows ? 0 : off[E];
   for (int r = (blockIdx.x * blockDim.x + threadIdx.x) / 32; r < rows; r += gridDim.x * blockDim.x / 32) {
     const int e = last_le(off, E + 1, r);
     const int d = e / El;
     const int64_t dst_row = pos[e] + (r - off[e]);
+    if (dst_row >= cap[d]) {  // the destination's buffer is smaller than this rank assumed
+      if (lane == 0) record_status(status, BS_ERR_CAPACITY);
+      continue;
+    }
     const uint4* src = x + (int64_t)token_of_row[r] * vecs;
     uint4* dst = at<uint4>(bases[d], L.recv) + dst_row * vecs;
     for (int64_t v = lane; v < vecs; v += 32) dst[v] = src[v];
@@ -184,7 +213,7 @@ __global__ void __launch_bounds__(256) ep_scatter_kernel(const uint4* __restrict
 // Wait for every rank's flag of `group`; with El > 0 also write the local
 // expert offsets of recv (expert-major over the counts matrix).
 __global__ void ep_arrived_kernel(uint64_t mine, EPLayout L, int group, int R, int E, int me, int El,
-                                  int* __restrict__ local_offsets, int* status) {
+                                  int cap_rows, int* __restrict__ local_offsets, int* status) {
   __shared__ int ok;
   if (threadIdx.x == 0) {
     const uint32_t* flags = at<uint32_t>(mine, L.flags);
@@ -195,17 +224,19 @@ __global__ void ep_arrived_kernel(uint64_t mine, EPLayout L, int group, int R, i
   const volatile int* cm = at<int>(mine, L.counts);
   int run = 0;
   for (int e = 0; e < El; ++e) {
-    local_offsets[e] = run;
+    local_offsets[e] = min(run, cap_rows);
     for (int s = 0; s < R; ++s) run += cm[s * E + me * El + e];
   }
-  local_offsets[El] = run;
+  if (run > cap_rows) record_status(status, BS_ERR_CAPACITY);  // the GEMMs then stop at cap_rows
+  local_offsets[El] = min(run, cap_rows);
 }
 
 // Dynamic shared memory: counts [R][E], loc [El + 1], seg [El][R + 1], src [El][R] (ints).
 __global__ void __launch_bounds__(256) ep_return_kernel(const uint4* __restrict__ y, int64_t vecs,
                                                         const uint64_t* __restrict__ bases, int R, int E,
-                                                        int me, EPLayout L) {
+                                                        int me, EPLayout L, int cap_rows, int* status) {
   extern __shared__ int sm[];
+  __shared__ int srcmax[kMaxRanks];  // every source's published src_rows
   const int El = E / R;
   int* cm = sm;                    // [R][E]
   int* loc = cm + R * E;           // [El + 1]: expert-major start of local expert e
@@ -214,6 +245,8 @@ __global__ void __launch_bounds__(256) ep_return_kernel(const uint4* __restrict_
   const uint64_t mine = bases[me];
   const volatile int* cmg = at<int>(mine, L.counts);
   for (int i = threadIdx.x; i < R * E; i += blockDim.x) cm[i] = cmg[i];
+  for (int s = threadIdx.x; s < R; s += blockDim.x)
+    srcmax[s] = (int)*reinterpret_cast<const volatile uint32_t*>(at<uint32_t>(bases[s], L.flags) + kSrcRows);
   __syncthreads();
   if (threadIdx.x == 0) {
     int run = 0;
@@ -237,12 +270,16 @@ __global__ void __launch_bounds__(256) ep_return_kernel(const uint4* __restrict_
   }
   __syncthreads();
   const int lane = threadIdx.x & 31;
-  const int rows = loc[El];
+  const int rows = min(loc[El], cap_rows);  // the GEMMs produced at most cap_rows rows
   for (int r = (blockIdx.x * blockDim.x + threadIdx.x) / 32; r < rows; r += gridDim.x * blockDim.x / 32) {
     const int e = last_le(loc, El + 1, r);
     const int within = r - loc[e];
     const int s = last_le(seg + e * (R + 1), R + 1, within);
     const int64_t dst_row = src[e * R + s] + (within - seg[e * (R + 1) + s]);
+    if (dst_row >= srcmax[s]) {  // beyond the source's yback
+      if (lane == 0) record_status(status, BS_ERR_CAPACITY);
+      continue;
+    }
     const uint4* a = y + (int64_t)r * vecs;
     uint4* b = at<uint4>(bases[s], L.yback) + dst_row * vecs;
     for (int64_t v = lane; v < vecs; v += 32) b[v] = a[v];
@@ -330,25 +367,29 @@ int bs_ep_p2p_free(void* base) {
 int bs_ep_p2p_dispatch(const void* x, int64_t H, const int32_t* expert_offsets, const int32_t* token_of_row,
                        void* my_base, const uint64_t* peer_bases, int64_t R, int64_t E, int64_t me,
                        int64_t cap_rows, int64_t src_rows, int32_t* local_offsets, void* stream) {
+  // every check comes before the first launch: once ep_counts_kernel runs,
+  // the peers expect this rank's rows for this epoch
   BS_TRY(check_shape(R, E, H, me));
   BS_ARG(x && expert_offsets && token_of_row && my_base && peer_bases && local_offsets,
          "bs_ep_p2p_dispatch: null pointer");
   BS_ALIGNED16(x, "x");
-  BS_ARG(cap_rows >= R * src_rows, "bs_ep_p2p_dispatch: cap_rows must hold every rank's rows (>= R * src_rows)");
-  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  const EPLayout L = ep_layout(R, E, H, cap_rows, src_rows);
-  int* status = device_status_ptr();
-  ep_counts_kernel<<<1, 256, 0, st>>>(expert_offsets, peer_bases, (int)R, (int)E, (int)me, L);
-  BS_CUDA(cudaGetLastError());
+  BS_ARG(src_rows >= 0 && cap_rows >= R * src_rows && cap_rows < (int64_t)INT32_MAX,
+         "bs_ep_p2p_dispatch: cap_rows must hold every rank's rows (>= R * src_rows)");
   const size_t smem = (size_t)(R * E + 2 * E + 1) * 4;
   BS_REQUIRE(smem <= 48 * 1024, BS_ERR_UNSUPPORTED, "bs_ep_p2p_dispatch: %lld ranks x %lld experts too large",
              (long long)R, (long long)E);
+  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const EPLayout L = ep_layout(R, E, H, cap_rows, src_rows);
+  int* status = device_status_ptr();
+  ep_counts_kernel<<<1, 256, 0, st>>>(expert_offsets, peer_bases, (int)R, (int)E, (int)me, L, (int)cap_rows,
+                                      (int)src_rows, status);
+  BS_CUDA(cudaGetLastError());
   ep_scatter_kernel<<<grid_rows(src_rows), 256, smem, st>>>(
       static_cast<const uint4*>(x), H / 8, expert_offsets, token_of_row, peer_bases, (int)R, (int)E, (int)me,
-      L, status);
+      L, (int)src_rows, status);
   BS_CUDA(cudaGetLastError());
   ep_arrived_kernel<<<1, 32, 0, st>>>(reinterpret_cast<uint64_t>(my_base), L, kRows, (int)R, (int)E, (int)me,
-                                      (int)(E / R), local_offsets, status);
+                                      (int)(E / R), (int)cap_rows, local_offsets, status);
   BS_CUDA(cudaGetLastError());
   return BS_OK;
 }
@@ -358,6 +399,8 @@ int bs_ep_p2p_return(const void* y, int64_t H, void* my_base, const uint64_t* pe
   BS_TRY(check_shape(R, E, H, me));
   BS_ARG(y && my_base && peer_bases, "bs_ep_p2p_return: null pointer");
   BS_ALIGNED16(y, "y");
+  BS_ARG(src_rows >= 0 && cap_rows >= R * src_rows && cap_rows < (int64_t)INT32_MAX,
+         "bs_ep_p2p_return: cap_rows must hold every rank's rows (>= R * src_rows)");
   const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const EPLayout L = ep_layout(R, E, H, cap_rows, src_rows);
   int* status = device_status_ptr();
@@ -366,10 +409,10 @@ int bs_ep_p2p_return(const void* y, int64_t H, void* my_base, const uint64_t* pe
   BS_REQUIRE(smem <= 48 * 1024, BS_ERR_UNSUPPORTED, "bs_ep_p2p_return: %lld ranks x %lld experts too large",
              (long long)R, (long long)E);
   ep_return_kernel<<<grid_rows(cap_rows), 256, smem, st>>>(static_cast<const uint4*>(y), H / 8, peer_bases,
-                                                            (int)R, (int)E, (int)me, L);
+                                                            (int)R, (int)E, (int)me, L, (int)cap_rows, status);
   BS_CUDA(cudaGetLastError());
   ep_arrived_kernel<<<1, 32, 0, st>>>(reinterpret_cast<uint64_t>(my_base), L, kResults, (int)R, (int)E, (int)me, 0,
-                                      nullptr, status);
+                                      (int)cap_rows, nullptr, status);
   BS_CUDA(cudaGetLastError());
   return BS_OK;
 }

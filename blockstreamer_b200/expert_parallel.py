@@ -32,6 +32,7 @@ pass, no library collective on the data path.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 from dataclasses import dataclass
 
@@ -39,6 +40,20 @@ import torch
 import torch.distributed as dist
 
 from . import _lib, kernels
+
+
+@contextlib.contextmanager
+def nvtx(name: str):
+    """An NVTX range around one stage's launches (seen by nsys / ncu; no cost
+    without a profiler attached)."""
+    if torch.cuda.is_available():
+        torch.cuda.nvtx.range_push(name)
+        try:
+            yield
+        finally:
+            torch.cuda.nvtx.range_pop()
+    else:
+        yield
 
 
 class CudaOps:
@@ -253,26 +268,82 @@ class ExpertParallelMoE:
         if T * k > ex.src_rows:
             raise ValueError(f"{T} tokens exceed the exchange's {ex.src_rows // k} per rank")
         self._mark("start")
-        sc, idx = self.ops.router(x, router_weight, router_bias, k)
+        with nvtx("ep.router"):
+            sc, idx = self.ops.router(x, router_weight, router_bias, k)
         self._mark("router")
-        d = kernels.dispatch(idx, self.E)
+        with nvtx("ep.dispatch"):
+            d = kernels.dispatch(idx, self.E)
         self._mark("dispatch")
-        ex.dispatch(x, d.expert_offsets, d.token_of_row)
+        with nvtx("ep.exchange_dispatch"):
+            ex.dispatch(x, d.expert_offsets, d.token_of_row)
         self._mark("exchange_dispatch")
         if self._h is None:
             I = p["gate_up_proj_blocks"].shape[1] // 2
             self._h = torch.empty(ex.cap, I, dtype=torch.bfloat16, device=x.device)
             self._y = torch.empty(ex.cap, H, dtype=torch.bfloat16, device=x.device)
         algo = getattr(self.ops, "algo", kernels.ALGO_AUTO)
-        kernels.moe_gate_up(ex.recv, ex.local_offsets, p["gate_up_proj_blocks"], p["gate_up_proj_scales"],
-                            p["gate_up_proj_bias"], alpha=self.alpha, limit=self.limit, algo=algo, out=self._h)
-        kernels.moe_down(self._h, ex.local_offsets, p["down_proj_blocks"], p["down_proj_scales"],
-                         p["down_proj_bias"], algo=algo, out=self._y)
+        with nvtx("ep.experts"):
+            kernels.moe_gate_up(ex.recv, ex.local_offsets, p["gate_up_proj_blocks"], p["gate_up_proj_scales"],
+                                p["gate_up_proj_bias"], alpha=self.alpha, limit=self.limit, algo=algo,
+                                out=self._h)
+            kernels.moe_down(self._h, ex.local_offsets, p["down_proj_blocks"], p["down_proj_scales"],
+                             p["down_proj_bias"], algo=algo, out=self._y)
         self._mark("experts")
-        ex.give_back(self._y)
+        with nvtx("ep.exchange_combine"):
+            ex.give_back(self._y)
         self._mark("exchange_combine")
-        out = kernels.combine(ex.yback[: T * k], d.row_of_slot, sc, T)
+        with nvtx("ep.combine"):
+            out = kernels.combine(ex.yback[: T * k], d.row_of_slot, sc, T)
         self._mark("combine")
         return out, sc, idx
+
+    def p2p_stages(self, x, router_weight, router_bias, p):
+        """The peer-memory layer as ordered (stage name, callable) pairs with
+        every buffer allocated once: calling them in order is one layer call
+        (the same kernels as ``forward``), and each can be captured in a CUDA
+        graph of its own to time the stages.  Returns (stages, out)."""
+        ex, k, E = self.exchange, self.top_k, self.E
+        if ex is None:
+            raise ValueError("p2p_stages needs the peer-memory exchange")
+        T, H = x.shape
+        dev = x.device
+        I = p["gate_up_proj_blocks"].shape[1] // 2
+        lib = _lib.load()
+        sc = torch.empty(T, k, dtype=torch.float32, device=dev)
+        idx = torch.empty(T, k, dtype=torch.int32, device=dev)
+        rws = torch.empty(max(lib.bs_router_workspace_bytes(T, H, E, _lib.BS_F32), 16), dtype=torch.uint8,
+                          device=dev)
+        d = kernels.Dispatch(torch.empty(E + 1, dtype=torch.int32, device=dev),
+                             torch.empty(T * k, dtype=torch.int32, device=dev),
+                             torch.empty(T * k, dtype=torch.int32, device=dev), None)
+        dws = torch.empty(max(lib.bs_dispatch_workspace_bytes(T, k, E), 16), dtype=torch.uint8, device=dev)
+        h = torch.empty(ex.cap, I, dtype=torch.bfloat16, device=dev)
+        y = torch.empty(ex.cap, H, dtype=torch.bfloat16, device=dev)
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+        algo = getattr(self.ops, "algo", kernels.ALGO_AUTO)
+
+        def router():
+            kernels.router(x, router_weight, router_bias, k, out_scores=sc, out_indices=idx, workspace=rws)
+
+        def dispatch():
+            kernels.dispatch(idx, E, out=d, workspace=dws)
+
+        def exchange_dispatch():
+            ex.dispatch(x, d.expert_offsets, d.token_of_row)
+
+        def experts():
+            kernels.moe_gate_up(ex.recv, ex.local_offsets, p["gate_up_proj_blocks"], p["gate_up_proj_scales"],
+                                p["gate_up_proj_bias"], alpha=self.alpha, limit=self.limit, algo=algo, out=h)
+            kernels.moe_down(h, ex.local_offsets, p["down_proj_blocks"], p["down_proj_scales"],
+                             p["down_proj_bias"], algo=algo, out=y)
+
+        def exchange_combine():
+            ex.give_back(y)
+
+        def combine():
+            kernels.combine(ex.yback[: T * k], d.row_of_slot, sc, T, out=out)
+
+        return [("router", router), ("dispatch", dispatch), ("exchange_dispatch", exchange_dispatch),
+                ("experts", experts), ("exchange_combine", exchange_combine), ("combine", combine)], out
 
     __call__ = forward

@@ -109,16 +109,20 @@ int bs_dispatch(const void* indices, int index_dtype, int64_t T, int64_t k, int6
  * held in a fixed 512 KiB device array inside the library instead of a caller
  * workspace.  No counterpart in the reference (its dispatch is Python that
  * allocates freely).  It serves callers that cannot allocate device memory
- * where they dispatch: code inside a CUDA graph capture, serving loops that
- * must not stall on cudaMalloc/cudaFree, runtimes whose pools own all device
- * memory, and ctypes/cgo/JNI callers without a device allocator.
+ * where they dispatch: serving loops that must not stall on the device-wide
+ * synchronization cudaMalloc/cudaFree imply, runtimes whose pools own all
+ * device memory, and ctypes/cgo/JNI callers without a device allocator to
+ * hand a workspace from.
  * Limits: 2 * ceil(T/256) * E * 4 bytes <= 512 KiB (e.g. T <= 65536 tokens
- * with E <= 256), else BS_ERR_CAPACITY.  It allocates nothing; the first call
- * on each device looks up the array's device address (make that first call
- * before any stream capture).  Every call on a device shares the one array:
- * calls whose kernels overlap on the GPU (different streams without ordering)
- * race and give wrong results; the array keeps the last call's contents, which
- * every call fully rewrites before reading. */
+ * with E <= 256), else BS_ERR_CAPACITY.  It calls no allocating routine.  The
+ * first call on each device looks up the array's device address with that
+ * device current and caches it for the process (make that first call before
+ * any stream capture; after a cudaDeviceReset the cached address is stale, so
+ * do not use this entry point in a process that resets a device it used).
+ * Every call on a device shares the one array: calls whose kernels overlap on
+ * the GPU (different streams without ordering) race and give wrong results;
+ * the array keeps the last call's contents, which every call fully rewrites
+ * before reading. */
 int bs_dispatch_noalloc(const void* indices, int index_dtype, int64_t T, int64_t k, int64_t E,
                         const void* x, int64_t H, int32_t* expert_offsets, int32_t* row_of_slot,
                         int32_t* token_of_row, void* x_perm, void* stream);
@@ -195,7 +199,14 @@ int bs_gather_rows(const void* src, const int32_t* row_map, int64_t rows, int64_
  *     it returns on the stream, this rank's yback is complete (combine it with
  *     row_of_slot).
  * Every wait for a peer is bounded (~2 s); a timeout is reported through
- * bs_device_status as BS_ERR_TIMEOUT. */
+ * bs_device_status as BS_ERR_TIMEOUT.
+ * Sizes: every rank must dispatch at most src_rows rows (tokens * k <=
+ * src_rows, i.e. expert_offsets[E] <= src_rows).  The kernels enforce it: a
+ * rank with more rows sends none (its peers see zero rows from it), and every
+ * row that would land beyond the destination's cap_rows, or a result beyond
+ * its source's src_rows (each rank publishes its own sizes in its buffer), is
+ * skipped; each case records BS_ERR_CAPACITY in the status word, so a wrong
+ * size never writes outside a peer's buffer. */
 size_t bs_ep_p2p_bytes(int64_t R, int64_t E, int64_t H, int64_t cap_rows, int64_t src_rows);
 int bs_ep_p2p_layout(int64_t R, int64_t E, int64_t H, int64_t cap_rows, int64_t src_rows,
                      size_t* recv_offset, size_t* yback_offset);

@@ -41,7 +41,8 @@ def dequant_expert(blocks: torch.Tensor, scales: torch.Tensor, dtype: torch.dtyp
 
     Exact product in float64, rounded once to ``dtype`` (products >= 2**128 go to
     +-inf). This equals transformers' LUT + ldexp result bit for bit
-    (integrations/mxfp4.py:305-330; pinned by tests/test_oracle.py).
+    (integrations/mxfp4.py:305-330; pinned by tests/test_oracle.py).  Runs on
+    the tensors' device (a test may evaluate the oracle where its inputs are).
     """
     rows, groups, _ = blocks.shape
     b = blocks.to(torch.int64)
@@ -50,8 +51,8 @@ def dequant_expert(blocks: torch.Tensor, scales: torch.Tensor, dtype: torch.dtyp
     # needs the wider type because 2**128 itself overflows float32.
     wide = bool((scales == 255).any())
     ft = torch.float64 if wide else torch.float32
-    lut = _FP4.to(ft)
-    vals = torch.empty(rows, groups, 32, dtype=ft)
+    lut = _FP4.to(device=blocks.device, dtype=ft)
+    vals = torch.empty(rows, groups, 32, dtype=ft, device=blocks.device)
     vals[..., 0::2] = lut[b & 0x0F]
     vals[..., 1::2] = lut[b >> 4]
     vals = vals * torch.pow(2.0, (scales.to(torch.int64) - 127).unsqueeze(-1).to(ft))
@@ -146,18 +147,25 @@ def experts_port(hidden: torch.Tensor, indices: torch.Tensor, weights: torch.Ten
 
 def experts_fp32(hidden: torch.Tensor, indices: torch.Tensor, weights: torch.Tensor,
                  p: Mapping[str, torch.Tensor], limit: float = LIMIT, alpha: float = ALPHA,
-                 return_intermediates: bool = False):
+                 return_intermediates: bool = False, experts_subset=None):
     """The reference math with every value in fp32; returns out [T, H] fp32.
 
     With ``return_intermediates`` also returns a dict keyed by expert with the
     (token_idx, top_k_pos, h [rows, I] fp32, y [rows, H] fp32) of each hit expert.
+    ``experts_subset`` restricts the loop to the given experts (``out`` then
+    holds only their contributions).  Evaluated on ``hidden``'s device (every
+    input must be there); fp32 matmuls must not be run in TF32.
     """
     x = hidden.float()
     T, H = x.shape
     E = p["gate_up_proj_blocks"].shape[0]
-    out = torch.zeros(T, H, dtype=torch.float32)
+    out = torch.zeros(T, H, dtype=torch.float32, device=x.device)
     inter = {}
-    for e in sorted(set(indices.reshape(-1).tolist())):
+    hit = sorted(set(indices.reshape(-1).tolist()))
+    if experts_subset is not None:
+        keep = set(int(e) for e in experts_subset)
+        hit = [e for e in hit if e in keep]
+    for e in hit:
         if e == E:
             continue
         top_k_pos, token_idx = expert_rows(indices, e)

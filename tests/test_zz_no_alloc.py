@@ -1,10 +1,10 @@
 """The allocation-free dispatch entry point (bs_dispatch_noalloc).
 
-Callers that cannot allocate device memory where they dispatch tokens (inside
-a CUDA graph capture, in serving loops that must not stall on cudaMalloc, in
-runtimes whose pools own all device memory, or from ctypes/cgo/JNI without an
-allocator) use this entry point: its scratch lives in a fixed device array of
-the library.  These tests call it through the C ABI and check it against
+Callers that cannot allocate device memory where they dispatch tokens
+(serving loops that must not stall on the synchronization cudaMalloc implies,
+runtimes whose pools own all device memory, or ctypes/cgo/JNI hosts without
+an allocator) use this entry point: its scratch lives in a fixed device array
+of the library.  These tests call it through the C ABI and check it against
 bs_dispatch (the workspace form) on two calls in a row — the second call must
 not be affected by what the first left in the shared array.  This file sorts
 last so that a run stopping at the first failure has run every other test.
