@@ -329,7 +329,7 @@ def run_reference(args, rank, world):
 STAGES = ("router", "dispatch", "gate_up", "down", "combine")
 LAUNCHES = {"router": 3, "dispatch": 4, "gate_up": 1, "down": 1, "combine": 1}  # router: 2 at T <= 64
 ALGOS = {"auto": kernels.ALGO_AUTO, "gemv": kernels.ALGO_GEMV, "tcgen05": kernels.ALGO_TCGEN05,
-         "mx": kernels.ALGO_MX}
+         "mx": kernels.ALGO_MX, "fused": kernels.ALGO_FUSED}
 
 
 def layer_stages(x, p, k, algo, bufs):
@@ -512,8 +512,10 @@ def measure(workload, args, world, local):
     k, E, H, I = shape.top_k, shape.experts, shape.hidden, shape.intermediate
     dev = torch.device("cuda", torch.cuda.current_device())
     algo = ALGOS[args.algo]
-    # the decode path: one bs_moe_forward call = 4 launches (route, gate_up, down, combine)
-    mx_path = algo == kernels.ALGO_MX or (algo == kernels.ALGO_AUTO and T <= 64)
+    # the decode paths: one bs_moe_forward call = one cooperative launch (T <= 8,
+    # fused) or 4 launches (route, gate_up, down, combine)
+    fused_path = algo == kernels.ALGO_FUSED or (algo == kernels.ALGO_AUTO and T <= 8)
+    mx_path = fused_path or algo == kernels.ALGO_MX or (algo == kernels.ALGO_AUTO and T <= 64)
     p = make_layer(shape, case_id, device=dev)
     x = make_tokens(T, H, case_id, device=dev)
     gu = (p["experts.gate_up_proj_blocks"], p["experts.gate_up_proj_scales"], p["experts.gate_up_proj_bias"])
@@ -551,7 +553,7 @@ def measure(workload, args, world, local):
     del flush_buf
 
     # per-stage breakdown: each C-ABI stage from its own graph replay.  The
-    # decode path's four launches sit inside one C call; its breakdown comes
+    # decode paths' launches sit inside one C call; their breakdown comes
     # from the ncu launch list instead.
     if mx_path:
         stage_ms = {"layer": ms}
@@ -593,9 +595,10 @@ def measure(workload, args, world, local):
                 "frac": achieved / peak, "traffic": None, "kernel": dom,
                 "peak_source": f"{peak_src} HBM copy bandwidth"}
         if dom == "layer":
-            roof["kernel"] = ("whole layer (route, gate_up, down, combine launches): weights of the "
-                              "touched experts + router weights + tokens over the device-timed step; "
-                              "a lower bound for the expert kernels, which move >97% of the bytes")
+            roof["kernel"] = (("whole layer, one cooperative kernel (decode_fused_kernel)" if fused_path else
+                               "whole layer (route, gate_up, down, combine launches)") +
+                              ": weights of the touched experts + router weights + tokens over the "
+                              "device-timed step; a lower bound for the expert streaming, >97% of the bytes")
     roof["algorithmic"] = {"flops": stage_flops.get(dom), "bytes": stage_bytes.get(dom), "launch_ms": stage_ms[dom]}
     layer_flops = algorithmic_flops(T, shape)
     layer_bytes = algorithmic_bytes(T, shape, distinct)
@@ -627,7 +630,7 @@ def measure(workload, args, world, local):
                                    "overlap step i's layer (double-buffered)") if pipelined else
                                   "none (decode size: copy, layer, copy back per step)"},
             "clocks": clk.summary(),
-            "gpu_launches": (4 if mx_path else sum(LAUNCHES.values())) * args.steps}
+            "gpu_launches": (1 if fused_path else 4 if mx_path else sum(LAUNCHES.values())) * args.steps}
 
 
 def run_ours(args, rank, world, local):

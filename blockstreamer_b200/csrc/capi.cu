@@ -49,6 +49,14 @@ int decode_forward(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, in
                    const void* dn_s, const void* dn_bias, int bias_f32, float alpha, float limit,
                    void* out, void* ws, cudaStream_t st,
                    const void* residual = nullptr);
+// Fused decode kernel (decode_fused.cu): the whole layer in one cooperative launch, T <= 8.
+bool fused_supported(int64_t T, int64_t H, int64_t I, int64_t E, int64_t k, float alpha, float limit,
+                     const void* gu_b, const void* gu_s, const void* dn_b, const void* dn_s);
+size_t fused_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t k);
+int fused_forward(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, int64_t k, const void* rw,
+                  const void* rb, int rdt, float* scores, int32_t* indices, const void* gu_b, const void* gu_s,
+                  const void* gu_bias, const void* dn_b, const void* dn_s, const void* dn_bias, int bias_f32,
+                  float alpha, float limit, void* out, void* ws, cudaStream_t st, const void* residual);
 
 namespace {
 
@@ -191,6 +199,7 @@ namespace {
 size_t moe_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t k) {
   size_t n = carve(nullptr, T, H, I, E, k).total;
   if (decode_supported(T, H, I, E, k)) n = std::max(n, decode_workspace_bytes(T, H, I, E, k));
+  if (T >= 1 && T <= 8 && k <= 8 && E <= 1024) n = std::max(n, fused_workspace_bytes(T, H, I, E, k));
   return n;
 }
 }  // namespace
@@ -215,11 +224,29 @@ int moe_forward_impl(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, 
   BS_ARG(T >= 0 && H > 0 && I > 0 && E > 0 && k > 0 && k <= E, "bs_moe_forward: bad sizes");
   BS_ARG((router_weight == nullptr) == (router_bias == nullptr),
          "bs_moe_forward: router weight and bias go together");
-  BS_ARG(algo >= BS_ALGO_AUTO && algo <= BS_ALGO_MX, "bs_moe_forward: unknown algo %d", algo);
+  BS_ARG(algo >= BS_ALGO_AUTO && algo <= BS_ALGO_FUSED, "bs_moe_forward: unknown algo %d", algo);
   if (T == 0) return BS_OK;
   BS_ARG(workspace, "bs_moe_forward: null workspace");
   BS_ALIGNED16(workspace, "workspace");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // AUTO takes the single-launch decode kernel wherever it applies (T <= 8)
+  const bool fused = algo == BS_ALGO_FUSED ||
+                     (algo == BS_ALGO_AUTO && fused_supported(T, H, I, E, k, alpha, limit, gate_up_blocks,
+                                                              gate_up_scales, down_blocks, down_scales));
+  if (fused) {
+    BS_ARG(router_dtype == BS_F32 || router_dtype == BS_BF16 || !router_weight,
+           "bs_moe_forward: router dtype must be bf16 or f32");
+    BS_ARG(bias_dtype == BS_BF16 || bias_dtype == BS_F32, "bs_moe_forward: bias dtype must be bf16 or f32");
+    BS_ARG(T <= 8 && k <= 8 && E <= 1024, "bs_moe_forward: BS_ALGO_FUSED needs T <= 8, k <= 8, E <= 1024");
+    const size_t need = fused_workspace_bytes(T, H, I, E, k);
+    BS_REQUIRE(workspace_bytes >= need, BS_ERR_CAPACITY,
+               "bs_moe_forward: workspace of %zu bytes is smaller than the %zu needed", workspace_bytes, need);
+    BS_TRY(check_device());
+    NvtxRange r("bs.fused_decode_layer");
+    return fused_forward(x, T, H, I, E, k, router_weight, router_bias, router_dtype, scores, indices,
+                         gate_up_blocks, gate_up_scales, gate_up_bias, down_blocks, down_scales, down_bias,
+                         bias_dtype == BS_F32, alpha, limit, out, workspace, st, residual);
+  }
   // AUTO takes the decode path whenever it applies (T <= 64, aligned blocks).
   const bool mx = algo == BS_ALGO_MX ||
                   (algo == BS_ALGO_AUTO && decode_supported(T, H, I, E, k) &&
@@ -294,10 +321,13 @@ extern "C" int bs_moe_decode(const void* x, int64_t T, int64_t H, int64_t I, int
                              const void* down_blocks, const void* down_scales, const void* down_bias,
                              int bias_dtype, float alpha, float limit, void* out, void* workspace,
                              size_t workspace_bytes, void* stream) {
+  const int algo = bs::fused_supported(T, H, I, E, k, alpha, limit, gate_up_blocks, gate_up_scales, down_blocks,
+                                       down_scales)
+                       ? BS_ALGO_FUSED
+                       : BS_ALGO_MX;
   return bs::moe_forward_impl(x, T, H, I, E, k, router_weight, router_bias, router_dtype, scores, indices,
                               gate_up_blocks, gate_up_scales, gate_up_bias, down_blocks, down_scales, down_bias,
-                              bias_dtype, alpha, limit, out, workspace, workspace_bytes, BS_ALGO_MX, stream,
-                              nullptr);
+                              bias_dtype, alpha, limit, out, workspace, workspace_bytes, algo, stream, nullptr);
 }
 
 extern "C" size_t bs_moe_block_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t k) {

@@ -161,7 +161,8 @@ def test_decode_matches_across_calls_and_graph():
 
 def test_bs_moe_decode_entry_point_matches_forward():
     """bs_moe_decode (the decode-shape C entry point) gives the same bits as
-    bs_moe_forward with BS_ALGO_MX, and rejects more than 64 tokens."""
+    bs_moe_forward's AUTO choice (the single-launch kernel at T <= 8, the
+    block-scaled path above), and rejects more than 64 tokens."""
     import ctypes
     from blockstreamer_b200 import _lib
     shape = LayerShape(512, 512, 32, 4)
@@ -171,10 +172,10 @@ def test_bs_moe_decode_entry_point_matches_forward():
                          "experts.down_proj_scales", "experts.down_proj_bias")]
     vp = lambda t: ctypes.c_void_p(t.data_ptr())
     lib = _lib.load()
-    for T in (1, 8):
+    for T in (1, 8, 20):
         x = make_tokens(T, shape.hidden, 12, device=DEV)
         ref, sc_ref, idx_ref = kernels.moe_forward(x, *pe, shape.top_k, router_weight=p["router.weight"],
-                                                   router_bias=p["router.bias"], algo=kernels.ALGO_MX)
+                                                   router_bias=p["router.bias"], algo=kernels.ALGO_AUTO)
         ws = torch.empty(lib.bs_moe_workspace_bytes(T, shape.hidden, shape.intermediate, shape.experts,
                                                     shape.top_k), dtype=torch.uint8, device=DEV)
         out = torch.empty_like(x)

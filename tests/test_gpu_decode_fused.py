@@ -1,0 +1,197 @@
+"""GPU parity of the single-launch decode kernel (BS_ALGO_FUSED, T <= 8).
+
+Against the reference's golden outputs and the fp32 oracle
+(block_streamer/gptoss.py:137-177, transformers modeling_gpt_oss.py:126-146):
+routing indices exact and weights within 1e-5 away from near-ties, layer
+output rel-L2 <= 5e-3 and max-abs <= 2e-2 * max|y| against fp32.  Shapes cover
+slices of one feature per CTA and CTAs with no feature at all (H, I < the SM
+count), partial 16-row tiles, k = 8, caller routing, a bf16 router, the
+decoder block's residual, wide-range activations, and determinism across
+calls and CUDA-graph replay.
+"""
+
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import GOLDEN
+from blockstreamer_b200 import kernels
+from blockstreamer_b200.synthetic import CASES, LayerShape, make_layer, make_tokens
+from oracle import moe as omoe
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+FUSED = kernels.ALGO_FUSED
+
+
+def experts_of(p):
+    return {k.split(".", 1)[1]: v for k, v in p.items() if k.startswith("experts.")}
+
+
+def check_close(out, ref, label):
+    rel = omoe.rel_l2(out.float(), ref.float())
+    mx = float((out.float() - ref.float()).abs().max())
+    scale = float(ref.float().abs().max())
+    print(f"{label}: rel_l2={rel:.3e} max_abs={mx:.3e} max_abs/max|y|={mx / scale:.3e}")
+    assert rel <= 5e-3, label
+    assert mx <= 2e-2 * scale, label
+
+
+def run(x, p, k, algo=FUSED, routed=True, indices=None, scores=None):
+    g = {n: t.to(DEV) for n, t in p.items()}
+    kw = dict(router_weight=g["router.weight"], router_bias=g["router.bias"]) if routed else \
+        dict(indices=indices.to(DEV), scores=scores.to(DEV))
+    out, sc, idx = kernels.moe_forward(
+        x.to(DEV), g["experts.gate_up_proj_blocks"], g["experts.gate_up_proj_scales"],
+        g["experts.gate_up_proj_bias"], g["experts.down_proj_blocks"], g["experts.down_proj_scales"],
+        g["experts.down_proj_bias"], k, algo=algo, **kw)
+    torch.cuda.synchronize()
+    assert kernels.device_status(clear=True) == 0
+    return out.cpu(), sc.cpu(), idx.cpu()
+
+
+@pytest.mark.parametrize("name,key", [("gptoss20b_t4", "gptoss20b"), ("gptoss120b_t3", "gptoss120b")])
+def test_fused_vs_reference_golden(name, key):
+    gold = np.load(os.path.join(GOLDEN, f"layer_{name}.npz"))
+    cid, T = int(gold["case"][0]), int(gold["tokens"][0])
+    shape = CASES[key]
+    p = make_layer(shape, cid)
+    x = make_tokens(T, shape.hidden, cid)
+    out, sc, idx = run(x, p, shape.top_k)
+    f64 = omoe.router_logits_f64(x, p["router.weight"], p["router.bias"])
+    keep = ~omoe.near_tie_tokens(f64, shape.top_k, 1e-6 + omoe.ROUTER_LOGIT_ERR, torch.from_numpy(gold["logits"]))
+    gi, gs = torch.from_numpy(gold["indices"]), torch.from_numpy(gold["scores"])
+    assert torch.equal(idx.long()[keep], gi[keep])
+    assert torch.allclose(sc[keep], gs[keep], atol=1e-5, rtol=0)
+    f32 = omoe.experts_fp32(x, gi, gs, experts_of(p))
+    check_close(out[keep], f32[keep], f"fused {name}")
+    ref = torch.from_numpy(gold["out_bits"].astype(np.int16)).view(torch.bfloat16).float()
+    assert omoe.rel_l2(out.float(), f32) <= max(2 * omoe.rel_l2(ref, f32), 1e-3)
+
+
+@pytest.mark.parametrize("T", [1, 2, 5, 8])
+@pytest.mark.parametrize("H,I,E,k", [(512, 512, 32, 4), (320, 448, 8, 2), (256, 256, 16, 8), (64, 64, 4, 2),
+                                     (2880, 2880, 32, 4)])
+def test_fused_random_routing_vs_fp32(T, H, I, E, k):
+    shape = LayerShape(H, I, E, k, 120, 128)
+    p = make_layer(shape, 70 + T)
+    x = make_tokens(T, H, 70 + T)
+    g = torch.Generator().manual_seed(T * 13 + H)
+    idx = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)])
+    w = torch.softmax(torch.randn(T, k, generator=g), -1)
+    out, _, _ = run(x, p, k, routed=False, indices=idx, scores=w)
+    check_close(out, omoe.experts_fp32(x, idx, w, experts_of(p)), f"fused T={T} H={H} I={I} E={E} k={k}")
+
+
+@pytest.mark.parametrize("T", [1, 8])
+def test_fused_router_matches_oracle(T):
+    shape = CASES["gptoss120b"]
+    p = make_layer(shape, 11)
+    x = make_tokens(T, shape.hidden, 11)
+    out, sc, idx = run(x, p, shape.top_k)
+    lg, s_ref, i_ref = omoe.router(x.float(), p["router.weight"], p["router.bias"], shape.top_k)
+    keep = ~omoe.near_tie_tokens(omoe.router_logits_f64(x, p["router.weight"], p["router.bias"]), shape.top_k,
+                                 1e-6 + omoe.ROUTER_LOGIT_ERR, lg)
+    assert torch.equal(idx.long()[keep], i_ref[keep])
+    assert torch.allclose(sc[keep], s_ref[keep], atol=1e-5, rtol=0)
+    check_close(out[keep], omoe.experts_fp32(x, i_ref, s_ref, experts_of(p))[keep], f"fused 120b T={T}")
+
+
+def test_fused_bf16_router_rounds_logits_like_reference():
+    shape = LayerShape(512, 512, 32, 4)
+    p = make_layer(shape, 12)
+    p["router.weight"] = p["router.weight"].to(torch.bfloat16)
+    p["router.bias"] = p["router.bias"].to(torch.bfloat16)
+    x = make_tokens(6, shape.hidden, 12)
+    out, sc, idx = run(x, p, shape.top_k)
+    lg, s_ref, i_ref = omoe.router(x, p["router.weight"], p["router.bias"], shape.top_k)
+    f64 = omoe.router_logits_f64(x, p["router.weight"].float(), p["router.bias"].float())
+    keep = ~omoe.near_tie_tokens(f64, shape.top_k, 2e-2, lg.float())
+    assert torch.equal(idx.long()[keep], i_ref[keep])
+    check_close(out[keep], omoe.experts_fp32(x, i_ref, s_ref.float(), experts_of(p))[keep], "fused bf16 router")
+
+
+def test_fused_one_hot_expert_and_wide_range_activations():
+    """All 8 tokens on expert 5; activations spanning 2^-20..2^20 within a token."""
+    T, E, k = 8, 16, 2
+    shape = LayerShape(256, 256, E, k, 124, 130)
+    p = make_layer(shape, 91)
+    g = torch.Generator().manual_seed(3)
+    mag = torch.pow(2.0, torch.randint(-20, 21, (T, shape.hidden), generator=g).float())
+    x = (torch.randn(T, shape.hidden, generator=g) * mag).to(torch.bfloat16)
+    idx = torch.zeros(T, k, dtype=torch.long)
+    idx[:, 0] = 5
+    idx[:, 1] = torch.arange(T) % 4 + 8
+    w = torch.softmax(torch.randn(T, k, generator=g), -1)
+    out, _, _ = run(x, p, k, routed=False, indices=idx, scores=w)
+    check_close(out, omoe.experts_fp32(x, idx, w, experts_of(p)), "fused one-hot / wide range")
+
+
+def test_fused_block_forward_adds_residual():
+    import types
+    from blockstreamer_b200 import B200GptOssMoEBlock
+
+    shape = CASES["gptoss20b"]
+    T = 4
+    cfg = types.SimpleNamespace(hidden_size=shape.hidden, intermediate_size=shape.intermediate,
+                                num_local_experts=shape.experts, num_experts_per_tok=shape.top_k,
+                                swiglu_limit=7.0, rms_norm_eps=1e-5)
+    p = make_layer(shape, 8)
+    nw = (1.0 + 0.1 * torch.randn(shape.hidden, generator=torch.Generator().manual_seed(8))).float()
+    x = make_tokens(T, shape.hidden, 8)
+    v = x.float()
+    xn = (nw * (v * torch.rsqrt(v.pow(2).mean(-1, keepdim=True) + 1e-5))).to(torch.bfloat16)
+    blk = B200GptOssMoEBlock(cfg)
+    state = {"post_attention_layernorm.weight": nw}
+    state.update({"mlp." + n: t for n, t in p.items()})
+    blk.load_state_dict({n: t.to(DEV) for n, t in state.items()}, strict=True, assign=True)
+    out = blk(x.to(DEV).reshape(1, T, -1)).reshape(T, -1).cpu()
+    lg, s_ref, i_ref = omoe.router(xn.float(), p["router.weight"], p["router.bias"], shape.top_k)
+    ref = x.float() + omoe.experts_fp32(xn, i_ref, s_ref, experts_of(p))
+    keep = ~omoe.near_tie_tokens(omoe.router_logits_f64(xn, p["router.weight"], p["router.bias"]), shape.top_k,
+                                 1e-6 + omoe.ROUTER_LOGIT_ERR, lg)
+    check_close(out.float()[keep], ref[keep], "fused block + residual")
+    assert kernels.device_status(clear=True) == 0
+
+
+def test_fused_deterministic_across_calls_and_graph():
+    shape = CASES["gptoss120b"]
+    p = make_layer(shape, 5, device=DEV)
+    x = make_tokens(8, shape.hidden, 5, device=DEV)
+    args = (x, p["experts.gate_up_proj_blocks"], p["experts.gate_up_proj_scales"],
+            p["experts.gate_up_proj_bias"], p["experts.down_proj_blocks"], p["experts.down_proj_scales"],
+            p["experts.down_proj_bias"], shape.top_k)
+    kw = dict(router_weight=p["router.weight"], router_bias=p["router.bias"], algo=FUSED)
+    a = kernels.moe_forward(*args, **kw)[0].clone()
+    b = kernels.moe_forward(*args, **kw)[0].clone()
+    assert torch.equal(a, b)
+    auto = kernels.moe_forward(*args, router_weight=p["router.weight"], router_bias=p["router.bias"])[0]
+    assert torch.equal(a, auto)                      # AUTO picks this path at T <= 8
+    ws = torch.empty(1 << 24, dtype=torch.uint8, device=DEV)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        kernels.moe_forward(*args, workspace=ws, **kw)
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        c = kernels.moe_forward(*args, workspace=ws, **kw)[0]
+    for _ in range(3):
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(a, c)
+    assert kernels.device_status(clear=True) == 0
+
+
+def test_fused_rejects_unsupported_shapes():
+    shape = LayerShape(512, 512, 32, 4)
+    p = make_layer(shape, 13, device=DEV)
+    x = make_tokens(9, shape.hidden, 13, device=DEV)
+    with pytest.raises((ValueError, RuntimeError)):
+        kernels.moe_forward(x, p["experts.gate_up_proj_blocks"], p["experts.gate_up_proj_scales"],
+                            p["experts.gate_up_proj_bias"], p["experts.down_proj_blocks"],
+                            p["experts.down_proj_scales"], p["experts.down_proj_bias"], 4,
+                            router_weight=p["router.weight"], router_bias=p["router.bias"], algo=FUSED)
+    assert kernels.device_status(clear=True) == 0

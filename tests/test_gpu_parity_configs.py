@@ -5,8 +5,9 @@
   the 320-row tile with its second 128 x 64 MMA or a two-chunk split);
 * gpt-oss-20b prefill, 4096 tokens, 32 experts (config 2: ~512 rows per
   expert, several token chunks per expert);
-* gpt-oss-120b decode, 1 / 8 / 64 tokens (config 3: the block-scaled decode
-  path, with gathered activation rows above 16 tokens).
+* gpt-oss-120b decode, 1 / 8 / 64 tokens (config 3: the single-launch decode
+  kernel at 1 and 8 tokens, the block-scaled decode path at all three, with
+  gathered activation rows above 16 tokens).
 
 Each test runs the layer through the C ABI (``bs_moe_forward``, router
 included) and checks, following block_streamer/gptoss.py:137-177 and
@@ -19,9 +20,10 @@ transformers modeling_gpt_oss.py:126-130:
     experts fit in the test's time; matmuls in true fp32, TF32 off);
   * prefill, in addition: gate_up (h) and down (y) rows of six experts,
     including the one with the fewest and the one with the most rows, against
-    the fp32 oracle on the CPU; the combine against an fp32 recombination of
-    the kernel's own y rows (one bf16 rounding); and bs_moe_forward equal, bit
-    for bit, to the same kernels called stage by stage.
+    the fp32 oracle on the CPU; the combine against an exact (fp64)
+    recombination of the kernel's own y rows, within the fp32-sum and one-bf16-
+    rounding error bound; and bs_moe_forward equal, bit for bit, to the same
+    kernels called stage by stage.
 """
 
 import pytest
@@ -120,11 +122,13 @@ def test_prefill_parity_at_bench_config(key, case_id, T):
         check_close(h_c[rows], h_ref, f"{key} expert {e} ({len(rows)} rows) h")
         check_close(y_c[rows], y_ref, f"{key} expert {e} ({len(rows)} rows) y")
 
-    # combine: fp32 sum of the kernel's own y rows, one bf16 rounding
-    yk = y.float()[d.row_of_slot.long()].view(T, k, -1)
-    ref_c = (yk * sc.unsqueeze(-1)).sum(1).to(torch.bfloat16).float()
-    ulp = ref_c.abs() * 2.0 ** -7 + 1e-30
-    assert bool(((out.float() - ref_c).abs() <= ulp).all())
+    # combine: the kernel's own y rows summed exactly (fp64); the kernel's fp32
+    # sum of k terms is within k * 2^-24 * sum|w y| of it, and its one bf16
+    # rounding within 2^-8 of the value
+    yk = y.double()[d.row_of_slot.long()].view(T, k, -1) * sc.double().unsqueeze(-1)
+    ref_c = yk.sum(1)
+    tol = ref_c.abs() * 2.0 ** -8 + k * 2.0 ** -23 * yk.abs().sum(1) + 1e-30
+    assert bool(((out.double() - ref_c).abs() <= tol).all())
 
     # the whole layer against the fp32 oracle on the GPU's copy of the inputs
     ref = omoe.experts_fp32(x, idx.long(), sc, experts_of(p))
@@ -141,14 +145,21 @@ def test_decode_parity_at_bench_config(T):
     args = layer_args(p)
     out, sc, idx = kernels.moe_forward(x, *args, k, router_weight=p["router.weight"],
                                        router_bias=p["router.bias"], algo=kernels.ALGO_AUTO)
-    out_mx, sc_mx, idx_mx = kernels.moe_forward(x, *args, k, router_weight=p["router.weight"],
-                                                router_bias=p["router.bias"], algo=kernels.ALGO_MX)
+    # AUTO: the single-launch kernel at T <= 8, the block-scaled path above
+    algo = kernels.ALGO_FUSED if T <= 8 else kernels.ALGO_MX
+    out_a, sc_a, idx_a = kernels.moe_forward(x, *args, k, router_weight=p["router.weight"],
+                                             router_bias=p["router.bias"], algo=algo)
     torch.cuda.synchronize()
-    assert torch.equal(out, out_mx) and torch.equal(idx, idx_mx)
+    assert torch.equal(out, out_a) and torch.equal(idx, idx_a)
     check_routing(x, p, k, sc, idx)
     print(f"T={T}: {int(torch.unique(idx).numel())} distinct experts")
     ref = omoe.experts_fp32(x, idx.long(), sc, experts_of(p))
     check_close(out, ref, f"120b decode T={T} layer")
+    if T <= 8:   # the four-launch block-scaled path on the same inputs
+        out_mx, _, idx_mx = kernels.moe_forward(x, *args, k, router_weight=p["router.weight"],
+                                                router_bias=p["router.bias"], algo=kernels.ALGO_MX)
+        assert torch.equal(idx_mx, idx)
+        check_close(out_mx, ref, f"120b decode T={T} block-scaled path")
     # against the prefill kernels (tcgen05 grouped GEMM) on the same routing
     out_tc, _, _ = kernels.moe_forward(x, *args, k, indices=idx, scores=sc, algo=kernels.ALGO_TCGEN05)
     check_close(out_tc, ref, f"120b T={T} tcgen05 path")
