@@ -61,7 +61,6 @@ constexpr int kFThreads = (kCW + 1) * 32;  // + the producer warp
 constexpr int kSlots = 8;         // runs in flight (mbarrier pairs)
 constexpr int kMaxTiles = 4;      // 16-row tiles per run
 constexpr int kMaxBPW = 8;        // K blocks per compute warp (K <= 32 * kCW * kMaxBPW)
-constexpr int kXPad = 64;         // bytes of padding per token row of x (bank spread)
 constexpr long long kWaitLimit = 2000000000LL;  // ~1 s at 1.9 GHz
 
 struct FusedArgs {
@@ -84,16 +83,21 @@ struct FusedArgs {
   const __nv_bfloat16* residual;  // [T][H] or NULL
   unsigned* bar;           // workspace: grid barrier {count, generation}
   float* logits;           // workspace: [T][E]
-  __half* hbuf;            // workspace: [kMaxD][T][I] f16
+  uint8_t* hbuf;           // workspace: [kMaxD][T] rows of hrow_bytes (f16 h, padded)
   int* status;
   int T, H, I, E, k;
   int ring_bytes;          // dynamic shared memory layout: x rows, reduction, ring
-  int xrow_bytes;
+  int xrow_bytes;          // pitch of a token row of x in shared memory (H * 2 + 64)
+  int hrow_bytes;          // pitch of a token row of h, in hbuf and in shared memory (I * 2 + 64)
 };
 
-__device__ __forceinline__ float e8m0_f32(uint32_t s) {
-  return s == 0 ? __uint_as_float(0x00400000u) : __uint_as_float(s << 23);  // 2^(s-127); 255 -> inf
-}
+// 2^n exactly, for -126 <= n <= 127.
+__device__ __forceinline__ float pow2i(int n) { return __uint_as_float((uint32_t)(n + 127) << 23); }
+
+// 2^(s-127) for an e8m0 byte, in one shift: exact for s >= 1 (255 -> inf, as
+// the reference's ldexp); s = 0 (2^-127) becomes 0, a weight below 6 * 2^-127
+// whose products are far below every output's rounding.
+__device__ __forceinline__ float e8m0_fast(uint32_t s) { return __uint_as_float(s << 23); }
 
 __device__ __forceinline__ void cvt_e2m1x8_f16(uint32_t w, uint32_t& o0, uint32_t& o1, uint32_t& o2,
                                                uint32_t& o3) {
@@ -147,6 +151,30 @@ __device__ bool grid_sync(unsigned* bar, unsigned nblocks, int* status, volatile
   return true;
 }
 
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tmbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ void st_release_cta_shared(int* p, int v) {
+  asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(ptx::smem_addr(p)), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_cta_shared(const int* p) {
+  int v;
+  asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(ptx::smem_addr(p)) : "memory");
+  return v;
+}
+// Generic-proxy writes (other CTAs' h, ordered by the grid barrier) before
+// this thread's async-proxy (bulk copy) reads of them.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 __device__ __forceinline__ void named_sync(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
 }
@@ -181,6 +209,7 @@ struct FusedShared {
   float rred[kCW + 1][kFT]; // router reduction
   float out[kFT][kMaxTiles * 16];  // this CTA's output features, fp32
   int abort;
+  int phase2;               // set once the grid barrier before phase D passed
 };
 
 // Run j of this CTA: j < nG gate_up of expert dist[j], else down of dist[j - nG].
@@ -217,6 +246,135 @@ __device__ __forceinline__ float red_sum(const float* red, int row, int t) {
   return v;
 }
 
+// Byte offset of a down run's h rows behind its weights in the ring.
+__device__ __forceinline__ int h_offset(const Run& r) { return (r.code_bytes + r.env_bytes + 127) & ~127; }
+
+// The compute warps' work on one run: wait for its bytes, multiply its rows
+// with the tokens (gate_up: x; down: h, both in shared memory), reduce over
+// the warps, epilogue.  `dry` runs the same code on in-bounds shared memory
+// without waiting, loading from or storing to global memory: executed once
+// before the weights stream, it brings this code into the instruction cache
+// while HBM is idle (instruction fetches that miss while the weight stream
+// saturates HBM cost microseconds each).  Kept out of line: one copy of the
+// code serves every call.
+__device__ __noinline__ void consume(const FusedArgs& p, FusedShared& s, uint8_t* ring, const uint8_t* xs, float* red,
+                                     const Run r, int j, bool dry, int i0, int f0) {
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const int T = p.T;
+  const int slot = j % kSlots;
+  const int K = r.phase ? p.I : p.H;
+  const int kb = K / 2, G = K / 32;
+  const int ntile = (r.rows + 15) >> 4;
+  volatile int* abort = &s.abort;
+  bool ok = true;
+  if (!dry) {
+    ok = !*abort && ptx::mbar_wait(ptx::smem_addr(&s.full[slot]), (j / kSlots) & 1, abort, kWaitLimit);
+    ok = __all_sync(0xffffffffu, ok);
+    if (!ok && lane == 0) record_status(p.status, BS_ERR_TIMEOUT);
+  }
+  if (ok) {
+    const uint8_t* codes = ring + (dry ? 0 : s.place[slot]);
+    const uint8_t* scl = codes + r.code_bytes + r.s_skew;
+    const uint8_t* bb = r.phase ? codes + h_offset(r) : xs;
+    const int bp = r.phase ? p.hrow_bytes : p.xrow_bytes;
+    float tot[kMaxTiles][4];
+#pragma unroll
+    for (int tl = 0; tl < kMaxTiles; ++tl) tot[tl][0] = tot[tl][1] = tot[tl][2] = tot[tl][3] = 0.f;
+    // two K blocks per iteration (blk, blk + kCW) so that two independent
+    // chains (loads -> cvt -> mma -> mma -> scale) are in flight per tile; a
+    // missing second block reuses the first block's operands under a zero
+    // scale.  Rows past the run's end read its last row (in bounds, finite)
+    // and their results are never used.
+    const int nblk_iter = dry ? kCW : G;
+#pragma unroll 1
+    for (int blk = warp; blk < nblk_iter; blk += 2 * kCW) {
+      const bool two = blk + kCW < nblk_iter;
+      const int blk2 = two ? blk + kCW : blk;
+      uint4 bv = make_uint4(0u, 0u, 0u, 0u), bw = make_uint4(0u, 0u, 0u, 0u);
+      if (g < T) {
+        bv = *reinterpret_cast<const uint4*>(bb + g * bp + blk * 64 + 16 * q);
+        bw = *reinterpret_cast<const uint4*>(bb + g * bp + blk2 * 64 + 16 * q);
+      }
+#pragma unroll
+      for (int tl = 0; tl < kMaxTiles; ++tl) {
+        if (tl < ntile) {
+          const int r0 = min(tl * 16 + g, r.rows - 1), r1 = min(tl * 16 + g + 8, r.rows - 1);
+          const uint8_t* c0p = codes + r0 * kb + 4 * q;
+          const uint8_t* c1p = codes + r1 * kb + 4 * q;
+          const uint32_t wa = *reinterpret_cast<const uint32_t*>(c0p + blk * 16);
+          const uint32_t wb = *reinterpret_cast<const uint32_t*>(c1p + blk * 16);
+          const uint32_t wc = *reinterpret_cast<const uint32_t*>(c0p + blk2 * 16);
+          const uint32_t wd = *reinterpret_cast<const uint32_t*>(c1p + blk2 * 16);
+          const float sa = e8m0_fast(scl[r0 * G + blk]), sb = e8m0_fast(scl[r1 * G + blk]);
+          const float sc = two ? e8m0_fast(scl[r0 * G + blk2]) : 0.f;
+          const float sd = two ? e8m0_fast(scl[r1 * G + blk2]) : 0.f;
+          uint32_t a0, a1, a2, a3, b0, b1, b2, b3, c0, c1, c2, c3, d0, d1, d2, d3;
+          cvt_e2m1x8_f16(wa, a0, a1, a2, a3);
+          cvt_e2m1x8_f16(wb, b0, b1, b2, b3);
+          cvt_e2m1x8_f16(wc, c0, c1, c2, c3);
+          cvt_e2m1x8_f16(wd, d0, d1, d2, d3);
+          float acc[4], acd[4];
+          mma_f16_16816(acc, a0, b0, a1, b1, bv.x, bv.y, 0.f, 0.f, 0.f, 0.f);
+          mma_f16_16816(acd, c0, d0, c1, d1, bw.x, bw.y, 0.f, 0.f, 0.f, 0.f);
+          mma_f16_16816(acc, a2, b2, a3, b3, bv.z, bv.w, acc[0], acc[1], acc[2], acc[3]);
+          mma_f16_16816(acd, c2, d2, c3, d3, bw.z, bw.w, acd[0], acd[1], acd[2], acd[3]);
+          tot[tl][0] = fmaf(acc[0], sa, fmaf(acd[0], sc, tot[tl][0]));
+          tot[tl][1] = fmaf(acc[1], sa, fmaf(acd[1], sc, tot[tl][1]));
+          tot[tl][2] = fmaf(acc[2], sb, fmaf(acd[2], sd, tot[tl][2]));
+          tot[tl][3] = fmaf(acc[3], sb, fmaf(acd[3], sd, tot[tl][3]));
+        }
+      }
+    }
+#pragma unroll
+    for (int tl = 0; tl < kMaxTiles; ++tl)
+      if (tl < ntile)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) red[((warp * kMaxTiles + tl) * 4 + i) * 32 + lane] = tot[tl][i];
+  }
+  __syncwarp();
+  if (!dry && lane == 0) ptx::mbar_arrive(ptx::smem_addr(&s.freed[slot]));  // the run's bytes may be overwritten
+  if (!dry) named_sync(1, kCW * 32);
+  if (!*abort) {
+    const unsigned msk = dry ? 0xFFu : s.mask[r.d];
+    const int64_t e = dry ? 0 : s.dist[r.d];
+    if (r.phase == 0) {
+      // gate_up epilogue: bias, clamped SwiGLU; h in f16 for the routed tokens
+      const int np = r.rows >> 1;
+      for (int it = tid; it < np * T; it += kCW * 32) {
+        const int pr = it / T, t = it - pr * T;
+        if (!((msk >> t) & 1u)) continue;
+        const float xs_inv = pow2i(-s.xsh[t]);
+        const int64_t brow = e * 2 * p.I + 2 * (i0 + pr);
+        float gate = red_sum(red, 2 * pr, t) * xs_inv, up = red_sum(red, 2 * pr + 1, t) * xs_inv;
+        if (!dry) {
+          gate += load_bias(p.gu_bias, p.bias_f32, brow);
+          up += load_bias(p.gu_bias, p.bias_f32, brow + 1);
+        }
+        gate = fminf(gate, p.limit);
+        up = fminf(fmaxf(up, -p.limit), p.limit);
+        const float hv = (up + 1.0f) * __fdividef(gate, 1.0f + __expf(-p.alpha * gate));
+        const __half hh = __float2half_rn(hv * pow2i(p.h_shift));
+        if (!dry)
+          *reinterpret_cast<__half*>(p.hbuf + (int64_t)(r.d * T + t) * p.hrow_bytes + 2 * (int64_t)(i0 + pr)) = hh;
+      }
+    } else {
+      // down epilogue: bias, times the routing weight, summed per token in
+      // ascending expert order (each (token, feature) has one owner thread)
+      for (int it = tid; it < r.rows * T; it += kCW * 32) {
+        const int lf = it / T, t = it - lf * T;
+        if (!((msk >> t) & 1u)) continue;
+        float v = red_sum(red, lf, t) * pow2i(-p.h_shift);
+        if (!dry) {
+          v += load_bias(p.dn_bias, p.bias_f32, e * p.H + f0 + lf);
+          s.out[t][lf] = fmaf(s.wd[r.d][t], v, s.out[t][lf]);
+        }
+      }
+    }
+  }
+  if (!dry) named_sync(1, kCW * 32);
+}
+
 __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const __grid_constant__ FusedArgs p) {
   extern __shared__ __align__(128) uint8_t dsm[];
   __shared__ FusedShared s;
@@ -230,6 +388,7 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const __grid
 
   if (tid == 0) {
     s.abort = 0;
+    s.phase2 = 0;
     for (int i = 0; i < kSlots; ++i) {
       ptx::mbar_init(ptx::smem_addr(&s.full[i]), 1);
       ptx::mbar_init(ptx::smem_addr(&s.freed[i]), kCW);
@@ -308,7 +467,7 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const __grid
     const int t = i / vpr, v = i - t * vpr;
     uint4* a = reinterpret_cast<uint4*>(xs + t * p.xrow_bytes + v * 16);
     const uint4 q = *a;
-    const float sc = exp2f((float)s.xsh[t]);
+    const float sc = pow2i(s.xsh[t]);
     uint4 o;
     const uint32_t in[4] = {q.x, q.y, q.z, q.w};
     uint32_t outw[4];
@@ -321,7 +480,27 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const __grid
     *a = o;
   }
   __syncthreads();
-  if (p.rw && tid == 0) grid_sync(p.bar, nblk, p.status, abort);
+  if (tid == 0) {
+    if (p.rw) grid_sync(p.bar, nblk, p.status, abort);
+  } else if (warp != 0 && warp < kCW) {
+    // while thread 0 waits for every CTA's logits, the other compute warps
+    // run the run-processing and top-k code once on in-bounds shared memory
+    // (no global access, results discarded): their instruction fetches miss
+    // while HBM is idle instead of once the weights saturate it
+    Run dry{};
+    dry.rows = 16;
+    dry.code_bytes = 16 * (H / 2);
+    dry.env_bytes = 16 * (H / 32);
+    consume(p, s, ring, xs, red, dry, 0, true, 0, 0);
+    dry.phase = 1;
+    dry.code_bytes = 16 * (I / 2);
+    dry.env_bytes = 16 * (I / 32);
+    consume(p, s, ring, xs, red, dry, 0, true, 0, 0);
+    if (warp == 1) {
+      float* junk = red + 64 * 32;  // scratch for the discarded top-k
+      warp_topk_any([&](int e) { return red[e]; }, E, k, junk, reinterpret_cast<int*>(junk + 32));
+    }
+  }
   __syncthreads();
 
   // ---------------------------------------------------------------- K: top-k, dispatch (every CTA)
@@ -377,175 +556,102 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const __grid
   const int f0 = (int)((int64_t)c * H / nblk), f1 = (int)((int64_t)(c + 1) * H / nblk);
   const int gRows = 2 * (i1 - i0), dRows = f1 - f0;
   const int nG = gRows > 0 ? D : 0, nD = dRows > 0 ? D : 0, nRuns = nG + nD;
+  const int hbytes = T * p.hrow_bytes;  // a down run's h rows (all T tokens)
 
   if (warp == kCW) {
     // ---------------------------------------------------------------- producer
+    // Places run j's weights in the ring as soon as space frees (down runs
+    // included, long before phase D), and a down run's h rows once the grid
+    // barrier before phase D has passed.  Never blocks: it polls the
+    // consumers' release barriers and the phase flag, bounded overall.
     if (lane == 0) {
-      int head = 0, lo = 0, issued = 0;
+      int j = 0, hn = nG, lo = 0, head = 0;
       int start[kSlots];
-      for (int j = 0; j < nRuns && !*abort; ++j) {
-        const Run r = run_of(p, s, j, nG, i0, gRows, f0, dRows);
-        const int need = (r.code_bytes + r.env_bytes + 127) & ~127;
-        int pos = -1;
-        while (pos < 0 && !*abort) {
-          if (j - lo < kSlots) {
-            if (j == lo) {
-              head = 0;
-              pos = 0;
-            } else {
-              const int tail = start[lo % kSlots];
-              // head == tail only when the ring is empty: a placement never
-              // ends exactly at the tail
-              if (head > tail) {
-                if (head + need <= p.ring_bytes) pos = head;
-                else if (need < tail) pos = 0;
-              } else if (head + need < tail) {
-                pos = head;
-              }
+      bool ph2 = false;
+      long long t_last = clock64();
+      while ((j < nRuns || hn < j) && !*abort) {
+        bool progress = false;
+        while (lo < j && mbar_test(ptx::smem_addr(&s.freed[lo % kSlots]), (lo / kSlots) & 1)) {
+          ++lo;
+          progress = true;
+        }
+        if (!ph2) ph2 = ld_acquire_cta_shared(&s.phase2) != 0;
+        if (ph2 && hn < j) {
+          fence_proxy_async_global();
+          const Run r = run_of(p, s, hn, nG, i0, gRows, f0, dRows);
+          ptx::bulk_load(ptx::smem_addr(ring + s.place[hn % kSlots] + h_offset(r)),
+                         p.hbuf + (int64_t)r.d * hbytes, (uint32_t)hbytes, ptx::smem_addr(&s.full[hn % kSlots]));
+          ++hn;
+          progress = true;
+        } else if (j < nRuns && j - lo < kSlots) {
+          const Run r = run_of(p, s, j, nG, i0, gRows, f0, dRows);
+          const int need = h_offset(r) + (r.phase ? ((hbytes + 127) & ~127) : 0);
+          int pos = -1;
+          if (j == lo) {
+            pos = 0;
+          } else {
+            // head == tail only when the ring is empty: a placement never
+            // ends exactly at the tail
+            const int tail = start[lo % kSlots];
+            if (head > tail) {
+              if (head + need <= p.ring_bytes) pos = head;
+              else if (need < tail) pos = 0;
+            } else if (head + need < tail) {
+              pos = head;
             }
           }
-          if (pos < 0) {  // wait until the oldest run in flight is consumed
-            if (!ptx::mbar_wait(ptx::smem_addr(&s.freed[lo % kSlots]), (lo / kSlots) & 1, abort, kWaitLimit)) {
-              record_status(p.status, BS_ERR_TIMEOUT);
-              break;
-            }
-            ++lo;
+          if (pos >= 0) {
+            start[j % kSlots] = pos;
+            head = pos + need;
+            s.place[j % kSlots] = pos;
+            const uint32_t fb = ptx::smem_addr(&s.full[j % kSlots]);
+            ptx::mbar_arrive_expect_tx(fb, (uint32_t)(r.code_bytes + r.env_bytes + (r.phase ? hbytes : 0)));
+            ptx::bulk_load(ptx::smem_addr(ring + pos), r.codes, (uint32_t)r.code_bytes, fb);
+            ptx::bulk_load(ptx::smem_addr(ring + pos + r.code_bytes), r.senv, (uint32_t)r.env_bytes, fb);
+            ++j;
+            progress = true;
           }
         }
-        if (pos < 0) break;
-        start[j % kSlots] = pos;
-        head = pos + need;
-        s.place[j % kSlots] = pos;
-        const uint32_t fb = ptx::smem_addr(&s.full[j % kSlots]);
-        ptx::mbar_arrive_expect_tx(fb, (uint32_t)(r.code_bytes + r.env_bytes));
-        ptx::bulk_load(ptx::smem_addr(ring + pos), r.codes, (uint32_t)r.code_bytes, fb);
-        ptx::bulk_load(ptx::smem_addr(ring + pos + r.code_bytes), r.senv, (uint32_t)r.env_bytes, fb);
-        issued = j + 1;
+        if (progress) {
+          t_last = clock64();
+        } else if (clock64() - t_last > kWaitLimit) {
+          record_status(p.status, BS_ERR_TIMEOUT);
+          *abort = 1;
+        } else {
+          __nanosleep(32);
+        }
+      }
+      // on an abort, complete every placed run's transaction count (their h
+      // rows may be stale then) so that the wait below finds every copy landed
+      for (; hn < j; ++hn) {
+        const Run r = run_of(p, s, hn, nG, i0, gRows, f0, dRows);
+        ptx::bulk_load(ptx::smem_addr(ring + s.place[hn % kSlots] + h_offset(r)), p.hbuf + (int64_t)r.d * hbytes,
+                       (uint32_t)hbytes, ptx::smem_addr(&s.full[hn % kSlots]));
       }
       // copies still in flight must land before the CTA exits
       volatile int quiet = 0;
-      for (int j = max(0, issued - kSlots); j < issued; ++j)
-        ptx::mbar_wait(ptx::smem_addr(&s.full[j % kSlots]), (j / kSlots) & 1, &quiet, 200000000LL);
+      for (int jj = max(0, j - kSlots); jj < j; ++jj)
+        ptx::mbar_wait(ptx::smem_addr(&s.full[jj % kSlots]), (jj / kSlots) & 1, &quiet, 200000000LL);
     }
     __syncwarp();
     return;
   }
 
   // ---------------------------------------------------------------- consumers (compute warps)
-  const int g = lane >> 2, q = lane & 3;
-  const float h_scale = exp2f((float)p.h_shift), h_unscale = exp2f(-(float)p.h_shift);
-  auto process = [&](int j) {
-    const Run r = run_of(p, s, j, nG, i0, gRows, f0, dRows);
-    const int slot = j % kSlots;
-    const int K = r.phase ? I : H;
-    const int kb = K / 2, G = K / 32;
-    const int ntile = (r.rows + 15) >> 4;
-    const unsigned msk = s.mask[r.d];
-    float tot[kMaxTiles][4];
-#pragma unroll
-    for (int tl = 0; tl < kMaxTiles; ++tl) tot[tl][0] = tot[tl][1] = tot[tl][2] = tot[tl][3] = 0.f;
-    bool ok = !*abort;
-    // down: the routed tokens' h (from L2, written by every CTA in phase G),
-    // all of this warp's blocks loaded before the wait
-    uint4 hb[kMaxBPW];
-#pragma unroll
-    for (int u = 0; u < kMaxBPW; ++u) {
-      hb[u] = make_uint4(0u, 0u, 0u, 0u);
-      const int blk = warp + u * kCW;
-      if (r.phase == 1 && ok && blk < G && ((msk >> g) & 1u))
-        hb[u] = __ldcg(reinterpret_cast<const uint4*>(p.hbuf + ((int64_t)(r.d * T + g) * I + blk * 32 + 8 * q)));
-    }
-    if (ok) ok = ptx::mbar_wait(ptx::smem_addr(&s.full[slot]), (j / kSlots) & 1, abort, kWaitLimit);
-    ok = __all_sync(0xffffffffu, ok);
-    if (ok) {
-      const uint8_t* codes = ring + s.place[slot];
-      const uint8_t* scl = codes + r.code_bytes + r.s_skew;
-#pragma unroll
-      for (int u = 0; u < kMaxBPW; ++u) {
-        const int blk = warp + u * kCW;
-        if (blk < G) {
-          uint4 bv = hb[u];
-          if (r.phase == 0) {
-            bv = make_uint4(0u, 0u, 0u, 0u);
-            if (g < T) bv = *reinterpret_cast<const uint4*>(xs + g * p.xrow_bytes + blk * 64 + 16 * q);
-          }
-#pragma unroll
-          for (int tl = 0; tl < kMaxTiles; ++tl) {
-            if (tl < ntile) {
-              const int r0 = tl * 16 + g, r1 = r0 + 8;
-              uint32_t wa = 0u, wb = 0u;
-              float sa = 0.f, sb = 0.f;
-              if (r0 < r.rows) {
-                wa = *reinterpret_cast<const uint32_t*>(codes + r0 * kb + blk * 16 + 4 * q);
-                sa = e8m0_f32(scl[r0 * G + blk]);
-              }
-              if (r1 < r.rows) {
-                wb = *reinterpret_cast<const uint32_t*>(codes + r1 * kb + blk * 16 + 4 * q);
-                sb = e8m0_f32(scl[r1 * G + blk]);
-              }
-              uint32_t a0, a1, a2, a3, c0, c1, c2, c3;
-              cvt_e2m1x8_f16(wa, a0, a1, a2, a3);
-              cvt_e2m1x8_f16(wb, c0, c1, c2, c3);
-              float acc[4];
-              mma_f16_16816(acc, a0, c0, a1, c1, bv.x, bv.y, 0.f, 0.f, 0.f, 0.f);
-              mma_f16_16816(acc, a2, c2, a3, c3, bv.z, bv.w, acc[0], acc[1], acc[2], acc[3]);
-              tot[tl][0] = fmaf(acc[0], sa, tot[tl][0]);
-              tot[tl][1] = fmaf(acc[1], sa, tot[tl][1]);
-              tot[tl][2] = fmaf(acc[2], sb, tot[tl][2]);
-              tot[tl][3] = fmaf(acc[3], sb, tot[tl][3]);
-            }
-          }
-        }
+  for (int j = 0; j <= nRuns; ++j) {
+    if (j == nG) {
+      // every CTA's h is written before any CTA reads it
+      named_sync(1, kCW * 32);
+      if (tid == 0) {
+        __threadfence();
+        grid_sync(p.bar, nblk, p.status, abort);
+        st_release_cta_shared(&s.phase2, 1);
       }
-#pragma unroll
-      for (int tl = 0; tl < kMaxTiles; ++tl)
-        if (tl < ntile)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) red[((warp * kMaxTiles + tl) * 4 + i) * 32 + lane] = tot[tl][i];
+      named_sync(1, kCW * 32);
     }
-    __syncwarp();
-    if (lane == 0) ptx::mbar_arrive(ptx::smem_addr(&s.freed[slot]));  // the run's shared memory is free
-    named_sync(1, kCW * 32);
-    if (!*abort) {
-      const int64_t e = s.dist[r.d];
-      if (r.phase == 0) {
-        // gate_up epilogue: bias, clamped SwiGLU; h in f16 for the routed tokens
-        const int np = r.rows >> 1;
-        for (int it = tid; it < np * T; it += kCW * 32) {
-          const int pr = it / T, t = it - pr * T;
-          if (!((msk >> t) & 1u)) continue;
-          const float xs_inv = exp2f(-(float)s.xsh[t]);
-          const int64_t brow = e * 2 * I + 2 * (i0 + pr);
-          float gate = red_sum(red, 2 * pr, t) * xs_inv + load_bias(p.gu_bias, p.bias_f32, brow);
-          float up = red_sum(red, 2 * pr + 1, t) * xs_inv + load_bias(p.gu_bias, p.bias_f32, brow + 1);
-          gate = fminf(gate, p.limit);
-          up = fminf(fmaxf(up, -p.limit), p.limit);
-          const float hv = (up + 1.0f) * __fdividef(gate, 1.0f + __expf(-p.alpha * gate));
-          p.hbuf[(int64_t)(r.d * T + t) * I + i0 + pr] = __float2half_rn(hv * h_scale);
-        }
-      } else {
-        // down epilogue: bias, times the routing weight, summed per token in
-        // ascending expert order (each (token, feature) has one owner thread)
-        for (int it = tid; it < r.rows * T; it += kCW * 32) {
-          const int lf = it / T, t = it - lf * T;
-          if (!((msk >> t) & 1u)) continue;
-          const float v = red_sum(red, lf, t) * h_unscale + load_bias(p.dn_bias, p.bias_f32, e * H + f0 + lf);
-          s.out[t][lf] = fmaf(s.wd[r.d][t], v, s.out[t][lf]);
-        }
-      }
-    }
-    named_sync(1, kCW * 32);
-  };
-
-  for (int j = 0; j < nG; ++j) process(j);
-  // every CTA's h is written before any CTA reads it
-  named_sync(1, kCW * 32);
-  if (tid == 0) {
-    __threadfence();
-    grid_sync(p.bar, nblk, p.status, abort);
+    if (j == nRuns) break;
+    consume(p, s, ring, xs, red, run_of(p, s, j, nG, i0, gRows, f0, dRows), j, false, i0, f0);
   }
-  named_sync(1, kCW * 32);
-  for (int j = nG; j < nRuns; ++j) process(j);
   named_sync(1, kCW * 32);
   for (int it = tid; it < T * dRows; it += kCW * 32) {
     const int t = it / dRows, lf = it - t * dRows;
@@ -561,9 +667,13 @@ __global__ void __launch_bounds__(kFThreads, 1) decode_fused_kernel(const __grid
 struct FusedWS {
   unsigned* bar;
   float* logits;
-  __half* hbuf;
+  uint8_t* hbuf;
   size_t total;
 };
+
+// Pitch of a token row of x (H) or h (I) in shared memory and of h in the
+// workspace: 64 bytes of padding spread the 8 token rows over the banks.
+inline int64_t token_row_bytes(int64_t n) { return n * 2 + 64; }
 
 FusedWS fused_carve(void* base, int64_t T, int64_t H, int64_t I, int64_t E, int64_t k) {
   (void)H;
@@ -577,7 +687,7 @@ FusedWS fused_carve(void* base, int64_t T, int64_t H, int64_t I, int64_t E, int6
   const int64_t dmax = std::min<int64_t>(E, T * k);
   w.bar = reinterpret_cast<unsigned*>(take(64));
   w.logits = reinterpret_cast<float*>(take((size_t)T * E * 4));
-  w.hbuf = reinterpret_cast<__half*>(take((size_t)dmax * T * I * 2));
+  w.hbuf = reinterpret_cast<uint8_t*>(take((size_t)dmax * T * token_row_bytes(I)));
   w.total = o;
   return w;
 }
@@ -594,7 +704,7 @@ int h_shift_for(float alpha, float limit) {
 }
 
 struct FusedPlan {
-  int grid, dyn_smem, ring_bytes, xrow_bytes;
+  int grid, dyn_smem, ring_bytes, xrow_bytes, hrow_bytes;
 };
 
 // Whether the fused decode kernel takes this layer, and its launch shape;
@@ -623,18 +733,24 @@ bool fused_plan(int64_t T, int64_t H, int64_t I, int64_t E, int64_t k, float alp
   cudaFuncAttributes fa{};
   if (cudaFuncGetAttributes(&fa, decode_fused_kernel) != cudaSuccess) return no("kernel attributes unavailable");
   const int grid = sm_count();
-  const int xrow = (int)(H * 2 + kXPad);
+  const int xrow = (int)token_row_bytes(H), hrow = (int)token_row_bytes(I);
   const int xbytes = (int)align_up((size_t)T * xrow, 128);
   const int red = kCW * kMaxTiles * 128 * 4;
   const int ring = ((optin - (int)fa.sharedSizeBytes - 1024 - xbytes - red) / 128) * 128;
   const int64_t g_rows = 2 * ((I + grid - 1) / grid), d_rows = (H + grid - 1) / grid;
   if (g_rows > kMaxTiles * 16 || d_rows > kMaxTiles * 16) return no("too many rows per CTA");
-  // largest run: codes + a 16-byte aligned envelope of its scales (+32 for the alignment)
-  const int64_t run_g = g_rows * (H / 2) + g_rows * (H / 32) + 32;
-  const int64_t run_d = d_rows * (I / 2) + d_rows * (I / 32) + 32;
-  if (ring <= 0 || std::max(run_g, run_d) + 128 > ring) return no("shared memory too small for one run");
+  // largest run: codes + a 16-byte aligned envelope of its scales (+32 for
+  // the alignment), rounded to 128; a down run also holds its tokens' h rows
+  // (the dry warm-up passes use 16 rows, fewer than any real run's bound)
+  const int64_t run_g = ((g_rows * (H / 2) + g_rows * (H / 32) + 32 + 127) / 128) * 128;
+  const int64_t run_d = ((d_rows * (I / 2) + d_rows * (I / 32) + 32 + 127) / 128) * 128 + ((T * hrow + 127) / 128) * 128;
+  const int64_t dry_d = ((16 * (I / 2) + 16 * (I / 32) + 127) / 128) * 128 + T * hrow;
+  const int64_t dry_g = 16 * (H / 2) + 16 * (H / 32);
+  if (ring <= 0 || std::max(std::max(run_g, run_d), std::max(dry_g, dry_d)) > ring)
+    return no("shared memory too small for one run");
   pl->grid = grid;
   pl->xrow_bytes = xrow;
+  pl->hrow_bytes = hrow;
   pl->ring_bytes = ring;
   pl->dyn_smem = xbytes + red + ring;
   return true;
@@ -693,6 +809,7 @@ int fused_forward(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, int
   a.T = (int)T, a.H = (int)H, a.I = (int)I, a.E = (int)E, a.k = (int)k;
   a.ring_bytes = pl.ring_bytes;
   a.xrow_bytes = pl.xrow_bytes;
+  a.hrow_bytes = pl.hrow_bytes;
   BS_CUDA(cudaFuncSetAttribute(decode_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.dyn_smem));
   int per_sm = 0;
   BS_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_fused_kernel, kFThreads, pl.dyn_smem));
