@@ -63,6 +63,13 @@ SIGNATURES = {
     "bs_moe_block_forward": (_i32, [_vp, _i64, _i64, _i64, _i64, _i64, _vp, _i32, _f32, _vp, _vp, _i32, _vp,
                                     _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _f32, _f32, _vp, _vp, _sz, _i32,
                                     _vp]),
+    "bs_moe_backward_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _i64]),
+    "bs_moe_backward": (_i32, [_vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _vp, _i32, _vp, _vp, _vp, _vp, _vp,
+                               _vp, _i32, _f32, _f32, _vp, _vp, _vp, _sz, _vp]),
+    "bs_router_backward": (_i32, [_vp, _i32, _i64, _i64, _i64, _i64, _vp, _i32, _vp, _vp, _vp, _vp, _vp, _vp,
+                                  _vp]),
+    "bs_mxfp4_matmul_backward_workspace_bytes": (_sz, [_i64, _i64]),
+    "bs_mxfp4_matmul_backward": (_i32, [_vp, _i64, _i64, _vp, _vp, _i64, _vp, _vp, _sz, _vp]),
     "bs_moe_forward": (_i32, [_vp, _i64, _i64, _i64, _i64, _i64, _vp, _vp, _i32, _vp, _vp,
                               _vp, _vp, _vp, _vp, _vp, _vp, _i32, _f32, _f32, _vp, _vp, _sz, _i32, _vp]),
 }

@@ -44,12 +44,11 @@ def dequantize_expert(blocks: Tensor, scales: Tensor, dtype: torch.dtype = torch
 
 
 class _MXFP4Matmul(torch.autograd.Function):
-    """x @ dequantize(blocks, scales) without keeping the dense weight.
+    """x @ dequantize(blocks, scales) without a dense weight in either direction.
 
-    Forward runs the fused dequant-GEMM kernel.  Backward (dL/dx) re-derives the
-    dense weight with the dequant kernel and multiplies by its transpose, as the
-    reference does (gptoss.py:64-71).
-    """
+    Forward: the fused dequant-GEMM kernel.  Backward (dL/dx, the role of
+    gptoss.py:64-71): the transposed tcgen05 GEMM over the packed codes
+    (bs_mxfp4_matmul_backward); nothing is saved but the packed tensors."""
 
     @staticmethod
     def forward(ctx, x: Tensor, blocks: Tensor, scales: Tensor) -> Tensor:
@@ -63,11 +62,11 @@ class _MXFP4Matmul(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad: Tensor):
         blocks, scales = ctx.saved_tensors
-        grad_x = None
-        if ctx.needs_input_grad[0]:
-            weight = dequantize_expert(blocks, scales, grad.dtype)
-            grad_x = grad @ weight.transpose(-2, -1)
-        return grad_x, None, None
+        if not ctx.needs_input_grad[0]:
+            return None, None, None
+        lead = grad.shape[:-1]
+        gx = kernels.mxfp4_matmul_backward(grad.reshape(-1, grad.shape[-1]), blocks.squeeze(0), scales.squeeze(0))
+        return gx.reshape(*lead, gx.shape[-1]).to(ctx.x_dtype), None, None
 
 
 def mxfp4_matmul(x: Tensor, blocks: Tensor, scales: Tensor) -> Tensor:
@@ -77,35 +76,67 @@ def mxfp4_matmul(x: Tensor, blocks: Tensor, scales: Tensor) -> Tensor:
     return _MXFP4Matmul.apply(x, blocks, scales)
 
 
-def _apply_gate(gate_up: Tensor, limit: float, alpha: float) -> Tensor:
-    """gptoss.py:130-135: clamped, interleaved SwiGLU in the tensor's dtype."""
-    gate = gate_up[..., ::2].clamp(max=limit)
-    up = gate_up[..., 1::2].clamp(min=-limit, max=limit)
-    return (up + 1) * (gate * torch.sigmoid(gate * alpha))
+class _ExpertsFunction(torch.autograd.Function):
+    """The expert layer as one differentiable op over the library's kernels.
+
+    Forward: bs_moe_forward with the caller's routing.  Backward (what the
+    reference gets from autograd through its per-expert loop,
+    gptoss.py:137-177 with 64-71): bs_moe_backward -- dL/dx and dL/d routing
+    weights from the recomputed intermediates and two transposed grouped
+    GEMMs, with no host synchronization.  Only x (bf16), the routing and the
+    module are kept for backward."""
+
+    @staticmethod
+    def forward(ctx, x: Tensor, weights: Tensor, indices: Tensor, m: "B200MXFP4Experts") -> Tensor:
+        xb = x.to(torch.bfloat16).contiguous()
+        idx = indices.to(torch.int32).contiguous()
+        w = weights.float().contiguous()
+        out, _, _ = kernels.moe_forward(
+            xb, m.gate_up_proj_blocks, m.gate_up_proj_scales, m.gate_up_proj_bias, m.down_proj_blocks,
+            m.down_proj_scales, m.down_proj_bias, idx.shape[1], indices=idx, scores=w, alpha=m.alpha,
+            limit=m.limit, algo=m.algo)
+        ctx.save_for_backward(xb, idx, w)
+        ctx.m = m
+        ctx.dtypes = (x.dtype, weights.dtype)
+        return out.to(x.dtype)
+
+    @staticmethod
+    def backward(ctx, grad: Tensor):
+        xb, idx, w = ctx.saved_tensors
+        m = ctx.m
+        g = grad.contiguous() if grad.dtype in (torch.bfloat16, torch.float32) else grad.float().contiguous()
+        gx, gw = kernels.moe_backward(xb, idx, w, g, m.gate_up_proj_blocks, m.gate_up_proj_scales,
+                                      m.gate_up_proj_bias, m.down_proj_blocks, m.down_proj_scales,
+                                      m.down_proj_bias, alpha=m.alpha, limit=m.limit)
+        dx = gx.to(ctx.dtypes[0]) if ctx.needs_input_grad[0] else None
+        dw = gw.to(ctx.dtypes[1]) if ctx.needs_input_grad[1] else None
+        return dx, dw, None, None
 
 
-def _experts_autograd(m: "B200MXFP4Experts", hidden: Tensor, indices: Tensor, weights: Tensor) -> Tensor:
-    """The expert loop of gptoss.py:137-177, step for step, for when gradients
-    are needed (dL/dx and dL/d routing weights): per hit expert, the fused
-    dequant-GEMM forward of ``mxfp4_matmul`` and, in backward, the dense weight
-    re-derived by the dequant kernel (gptoss.py:64-71).  Like the reference it
-    synchronizes with the host to find the hit experts and their rows."""
-    E = m.num_experts
-    next_states = torch.zeros_like(hidden)
-    with torch.no_grad():
-        mask = torch.nn.functional.one_hot(indices.long(), num_classes=E).permute(2, 1, 0)
-        hit = torch.greater(mask.sum(dim=(-1, -2)), 0).nonzero()
-    for entry in hit:
-        e = int(entry[0])
-        top_k_pos, token_idx = torch.where(mask[e])
-        current = hidden[token_idx]
-        gate_up = mxfp4_matmul(current, m.gate_up_proj_blocks[e:e + 1], m.gate_up_proj_scales[e:e + 1]) \
-            + m.gate_up_proj_bias[e]
-        gated = _apply_gate(gate_up, m.limit, m.alpha)
-        out = mxfp4_matmul(gated, m.down_proj_blocks[e:e + 1], m.down_proj_scales[e:e + 1]) + m.down_proj_bias[e]
-        out = out * weights[token_idx, top_k_pos, None]
-        next_states = next_states.index_add(0, token_idx, out.to(hidden.dtype))
-    return next_states
+class _RouterFunction(torch.autograd.Function):
+    """GptOssTopKRouter (modeling_gpt_oss.py:126-130) as one differentiable op:
+    forward on the library's router kernel (bf16 tokens, fp32 accumulate),
+    backward through the softmax over the k selected logits on
+    bs_router_backward (dL/dx, and dL/dW, dL/db when they require grad)."""
+
+    @staticmethod
+    def forward(ctx, x: Tensor, weight: Tensor, bias: Tensor, top_k: int):
+        xb = x.to(torch.bfloat16).contiguous()
+        _, scores, idx = kernels.router(xb, weight, bias, top_k, index_dtype=torch.int32)
+        ctx.save_for_backward(xb, weight, scores, idx)
+        ctx.x_dtype = x.dtype
+        ctx.mark_non_differentiable(idx)
+        return scores, idx
+
+    @staticmethod
+    def backward(ctx, grad_scores: Tensor, _grad_idx):
+        xb, weight, scores, idx = ctx.saved_tensors
+        gx, gW, gb = kernels.router_backward(xb, weight, scores, idx, grad_scores,
+                                             want_weight_grad=ctx.needs_input_grad[1],
+                                             want_bias_grad=ctx.needs_input_grad[2])
+        return (gx.to(ctx.x_dtype) if ctx.needs_input_grad[0] else None,
+                gW.to(weight.dtype) if gW is not None else None,
+                gb.to(weight.dtype) if gb is not None else None, None)
 
 
 def _packed(experts: int, rows: int, groups: int) -> nn.Parameter:
@@ -151,7 +182,7 @@ class B200MXFP4Experts(nn.Module):
         if router_indices is None or routing_weights is None:
             raise ValueError("B200MXFP4Experts needs router_indices and routing_weights")
         if torch.is_grad_enabled() and (hidden_states.requires_grad or routing_weights.requires_grad):
-            return _experts_autograd(self, hidden_states, router_indices, routing_weights)
+            return _ExpertsFunction.apply(hidden_states, routing_weights, router_indices, self)
         k = router_indices.shape[-1]
         out, _, _ = kernels.moe_forward(
             hidden_states.to(torch.bfloat16), self.gate_up_proj_blocks, self.gate_up_proj_scales,
@@ -189,16 +220,15 @@ class B200GptOssMLP(nn.Module):
     def forward(self, hidden_states: Tensor):
         B, S, H = hidden_states.shape
         ex = self.experts
+        router = self.router
         if torch.is_grad_enabled() and hidden_states.requires_grad:
-            # differentiable form: the HF router (modeling_gpt_oss.py:126-130)
-            # in torch ops, then the expert loop above
+            # differentiable form: router and experts as two autograd ops over
+            # the library's kernels (forward and backward on the GPU); the
+            # router's parameters get gradients too when they require them
             flat = hidden_states.reshape(-1, H)
-            logits = torch.nn.functional.linear(flat.to(self.router.weight.dtype), self.router.weight,
-                                                self.router.bias)
-            top_v, top_i = torch.topk(logits, self.top_k, dim=-1)
-            scores = torch.softmax(top_v, dim=1, dtype=top_v.dtype)
-            out = _experts_autograd(ex, flat, top_i, scores)
-            return out.reshape(B, S, H), scores
+            scores, idx = _RouterFunction.apply(flat, router.weight, router.bias, self.top_k)
+            out = _ExpertsFunction.apply(flat, scores, idx, ex)
+            return out.reshape(B, S, H), scores.to(router.weight.dtype)
         x = hidden_states.reshape(-1, H).to(torch.bfloat16)
         out, scores, _ = kernels.moe_forward(
             x, ex.gate_up_proj_blocks, ex.gate_up_proj_scales, ex.gate_up_proj_bias,

@@ -350,3 +350,75 @@ def moe_forward(x: torch.Tensor, gate_up_blocks, gate_up_scales, gate_up_bias, d
                   float(alpha), float(limit), _p(out), _p(workspace), workspace.numel(), algo,
                   _stream(x))
     return out, sc, idx
+
+
+def moe_backward(x: torch.Tensor, indices: torch.Tensor, weights: torch.Tensor, grad_out: torch.Tensor,
+                 gate_up_blocks, gate_up_scales, gate_up_bias, down_blocks, down_scales, down_bias,
+                 alpha=ALPHA, limit=LIMIT):
+    """dL/dx [T,H] f32 and dL/d routing weights [T,k] f32 of the expert layer
+    (bs_moe_backward): transposed tcgen05 grouped GEMMs over the packed
+    weights, no host synchronization."""
+    _cuda("moe_backward", x, indices, weights, grad_out, gate_up_blocks, gate_up_scales, down_blocks, down_scales)
+    if x.dtype != torch.bfloat16:
+        raise ValueError("moe_backward: x must be bf16")
+    if grad_out.dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("moe_backward: grad_out must be bf16 or f32")
+    x = _contig("x", x)
+    T, H = x.shape
+    k = indices.shape[1]
+    E, two_i = gate_up_blocks.shape[:2]
+    I = two_i // 2
+    dev = x.device
+    idx = indices.to(torch.int32).contiguous()
+    w = weights.float().contiguous()
+    go = _contig("grad_out", grad_out)
+    gx = torch.empty(T, H, dtype=torch.float32, device=dev)
+    gw = torch.empty(T, k, dtype=torch.float32, device=dev)
+    ws = torch.empty(max(_lib.load().bs_moe_backward_workspace_bytes(T, H, I, E, k), 16), dtype=torch.uint8,
+                     device=dev)
+    bias_code = _bias_code(gate_up_bias)
+    if down_bias is not None and down_bias.dtype != gate_up_bias.dtype:
+        down_bias = down_bias.to(gate_up_bias.dtype)
+    with torch.cuda.device(dev):
+        _lib.call("bs_moe_backward", _p(x), T, H, I, E, k, _p(idx), _p(w), _p(go), _DT[go.dtype],
+                  _p(gate_up_blocks), _p(gate_up_scales), _p(gate_up_bias), _p(down_blocks), _p(down_scales),
+                  _p(down_bias), bias_code, float(alpha), float(limit), _p(gx), _p(gw), _p(ws), ws.numel(),
+                  _stream(x))
+    return gx, gw
+
+
+def router_backward(x: torch.Tensor, weight: torch.Tensor, scores: torch.Tensor, indices: torch.Tensor,
+                    grad_scores: torch.Tensor, want_weight_grad: bool = False, want_bias_grad: bool = False):
+    """Backward of the router (bs_router_backward): returns (dL/dx f32 [T,H],
+    dL/dW f32 [E,H] or None, dL/db f32 [E] or None)."""
+    _cuda("router_backward", x, weight, scores, indices, grad_scores)
+    x = _contig("x", x)
+    T, H = x.shape
+    E = weight.shape[0]
+    k = indices.shape[1]
+    dev = x.device
+    gx = torch.zeros(T, H, dtype=torch.float32, device=dev)
+    gW = torch.zeros(E, H, dtype=torch.float32, device=dev) if want_weight_grad else None
+    gb = torch.zeros(E, dtype=torch.float32, device=dev) if want_bias_grad else None
+    with torch.cuda.device(dev):
+        _lib.call("bs_router_backward", _p(x), _DT[x.dtype], T, H, E, k, _p(_contig("weight", weight)),
+                  _DT[weight.dtype], _p(scores.float().contiguous()), _p(indices.to(torch.int32).contiguous()),
+                  _p(grad_scores.float().contiguous()), _p(gx), _p(gW), _p(gb), _stream(x))
+    return gx, gW, gb
+
+
+def mxfp4_matmul_backward(grad_out: torch.Tensor, blocks: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """dL/dx [m, K] bf16 of x @ dequant(W) for one expert W = blocks [N, K/32, 16]
+    (bs_mxfp4_matmul_backward: the transposed tcgen05 GEMM, no dense weight)."""
+    _cuda("mxfp4_matmul_backward", grad_out, blocks, scales)
+    go = _contig("grad_out", grad_out.to(torch.bfloat16))
+    m, N = go.shape
+    K = blocks.shape[1] * 32
+    out = torch.empty(m, K, dtype=torch.bfloat16, device=go.device)
+    lib = _lib.load()
+    ws = torch.empty(max(lib.bs_mxfp4_matmul_backward_workspace_bytes(N, K), 16), dtype=torch.uint8,
+                     device=go.device)
+    with torch.cuda.device(go.device):
+        _lib.call("bs_mxfp4_matmul_backward", _p(go), m, N, _p(_contig("blocks", blocks)),
+                  _p(_contig("scales", scales)), K, _p(out), _p(ws), ws.numel(), _stream(go))
+    return out

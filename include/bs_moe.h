@@ -272,6 +272,48 @@ int bs_moe_decode(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, int
                   int bias_dtype, float alpha, float limit, void* out, void* workspace,
                   size_t workspace_bytes, void* stream);
 
+/* Backward of the expert layer: dL/dx and dL/d routing weights of
+ *   out[t] = sum_s weights[t,s] * (SwiGLU(x[t] @ W_gu[e]^T + b_gu[e]) @ W_d[e]^T + b_d[e]),
+ *   e = indices[t,s]  -- i.e. autograd through block_streamer/gptoss.py:137-177
+ * with _MXFP4Matmul.backward (gptoss.py:64-71), which the reference runs as a
+ * per-expert loop over densely dequantized weights with host syncs.  Here:
+ * dispatch, the gate_up pre-activation, h and y recomputed by the forward
+ * kernels, dL/dw and dy in one pass, then two TRANSPOSED tcgen05 grouped
+ * GEMMs over the packed weights (dg = SwiGLU'(g) * (dy @ W_d), dx_perm =
+ * dg @ W_gu) and an fp32 sum over each token's slots; no host sync.
+ * x [T,H] bf16; indices [T,k] int32; weights [T,k] f32; grad_out [T,H] bf16
+ * or f32 (grad_dtype); grad_x [T,H] f32 and grad_weights [T,k] f32 are
+ * written (not accumulated).  H and 2I multiples of 64.
+ * Workspace: bs_moe_backward_workspace_bytes(T, H, I, E, k). */
+size_t bs_moe_backward_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t k);
+int bs_moe_backward(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, int64_t k,
+                    const int32_t* indices, const float* weights, const void* grad_out, int grad_dtype,
+                    const void* gate_up_blocks, const void* gate_up_scales, const void* gate_up_bias,
+                    const void* down_blocks, const void* down_scales, const void* down_bias,
+                    int bias_dtype, float alpha, float limit, float* grad_x, float* grad_weights,
+                    void* workspace, size_t workspace_bytes, void* stream);
+
+/* Backward of the router (transformers modeling_gpt_oss.py:126-130: logits =
+ * x W^T + b in the weight dtype, top-k, softmax over the k): from
+ * grad_scores [T,k] f32 and the forward's scores/indices, ACCUMULATES
+ * dL/dx into grad_x [T,H] f32 and, when non-NULL, dL/dW into grad_weight
+ * [E,H] f32 and dL/db into grad_bias [E] f32 (atomics).  x bf16 or f32
+ * (x_dtype), weight bf16 or f32 (w_dtype). */
+int bs_router_backward(const void* x, int x_dtype, int64_t T, int64_t H, int64_t E, int64_t k,
+                       const void* weight, int w_dtype, const float* scores, const int32_t* indices,
+                       const float* grad_scores, float* grad_x, float* grad_weight, float* grad_bias,
+                       void* stream);
+
+/* dL/dx of one expert projection (bs_mxfp4_matmul): grad_x [m,K] bf16 =
+ * grad_out [m,N] bf16 @ dequant(W) with W = blocks [N,K/32,16], scales
+ * [N,K/32] -- block_streamer/gptoss.py:64-71 without the dense weight (the
+ * transposed tcgen05 GEMM over the packed codes).  N a multiple of 64.
+ * Workspace: bs_mxfp4_matmul_backward_workspace_bytes(N, K). */
+size_t bs_mxfp4_matmul_backward_workspace_bytes(int64_t N, int64_t K);
+int bs_mxfp4_matmul_backward(const void* grad_out, int64_t m, int64_t N, const void* blocks,
+                             const void* scales, int64_t K, void* grad_x, void* workspace,
+                             size_t workspace_bytes, void* stream);
+
 /* RMSNorm of the gpt-oss decoder layer.  Replaces transformers
  * models/gpt_oss/modeling_gpt_oss.py GptOssRMSNorm.forward:
  *   out = bf16(weight * (float(x) * rsqrt(mean(float(x)^2) + eps)))

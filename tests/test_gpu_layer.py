@@ -139,8 +139,9 @@ def test_mxfp4_matmul_matches_dense(m, K, N, algo):
 
 
 def test_mxfp4_matmul_autograd_and_memory():
-    """Gradient equals grad @ W^T and no dense weight survives into backward
-    (tests/test_offload.py:390-402)."""
+    """Gradient equals grad @ W^T (here to bf16 rounding: the transposed GEMM
+    accumulates in fp32 from the packed codes) and no dense weight survives
+    into backward (tests/test_offload.py:390-402)."""
     from blockstreamer_b200 import dequantize_expert, mxfp4_matmul
     torch.manual_seed(0)
     blocks = torch.randint(0, 255, (1, 64, 4, 16), dtype=torch.uint8, device=DEV)
@@ -150,7 +151,8 @@ def test_mxfp4_matmul_autograd_and_memory():
     out = mxfp4_matmul(x, blocks, scales)
     grad = torch.randn_like(out)
     out.backward(grad)
-    assert torch.equal(x.grad, grad @ weight.t())
+    ref = grad.float() @ weight.float().t()
+    assert omoe.rel_l2(x.grad.float().cpu(), ref.cpu()) <= 4e-3
     torch.cuda.reset_peak_memory_stats()
     base = torch.cuda.memory_allocated()
     chained = [mxfp4_matmul(x, blocks, scales) for _ in range(64)]
