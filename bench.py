@@ -51,6 +51,8 @@ L2_BYTES = 126 * 1024 * 1024
 # ncu capture of the default workload; stored constants, not measured per run.
 NCU_TRAFFIC = {("gptoss120b-prefill-8192", "gate_up"): 1501327360,
                ("gptoss120b-prefill-8192", "down"): 924871936}
+# decode shapes: steps rotate over this many distinct layers (see measure())
+ROT_LAYERS = 8
 # a timed region shorter than this runs at the burst clock: its tensor-bound
 # kernels are compared with the burst (not the sustained) GEMM peak
 SUSTAINED_REGION_S = 1.0
@@ -512,9 +514,9 @@ def measure(workload, args, world, local):
     k, E, H, I = shape.top_k, shape.experts, shape.hidden, shape.intermediate
     dev = torch.device("cuda", torch.cuda.current_device())
     algo = ALGOS[args.algo]
-    # the decode paths: one bs_moe_forward call = one cooperative launch (T <= 8,
-    # fused) or 4 launches (route, gate_up, down, combine)
-    fused_path = algo == kernels.ALGO_FUSED or (algo == kernels.ALGO_AUTO and T <= 8)
+    # the decode paths: one bs_moe_forward call = 4 launches (route, gate_up,
+    # down, combine), or one cooperative launch with --algo fused (T <= 8)
+    fused_path = algo == kernels.ALGO_FUSED
     mx_path = fused_path or algo == kernels.ALGO_MX or (algo == kernels.ALGO_AUTO and T <= 64)
     p = make_layer(shape, case_id, device=dev)
     x = make_tokens(T, H, case_id, device=dev)
@@ -522,35 +524,63 @@ def measure(workload, args, world, local):
     dn = (p["experts.down_proj_blocks"], p["experts.down_proj_scales"], p["experts.down_proj_bias"])
     ws = torch.empty(kernels._lib.load().bs_moe_workspace_bytes(T, H, I, E, k), dtype=torch.uint8, device=dev)
 
-    def layer(xin, workspace=ws):
-        return kernels.moe_forward(xin, *gu, *dn, k, router_weight=p["router.weight"],
-                                   router_bias=p["router.bias"], algo=algo, workspace=workspace)
+    def layer_fn(lp):
+        lgu = (lp["experts.gate_up_proj_blocks"], lp["experts.gate_up_proj_scales"], lp["experts.gate_up_proj_bias"])
+        ldn = (lp["experts.down_proj_blocks"], lp["experts.down_proj_scales"], lp["experts.down_proj_bias"])
 
+        def call(xin, workspace=ws):
+            return kernels.moe_forward(xin, *lgu, *ldn, k, router_weight=lp["router.weight"],
+                                       router_bias=lp["router.bias"], algo=algo, workspace=workspace)
+        return call
+
+    layer = layer_fn(p)
     for _ in range(args.warmup):
         out, sc, idx = layer(x)
     torch.cuda.synchronize()
-    step = lambda: layer(x)  # noqa: E731
+    distinct = int(torch.unique(idx).numel())
+    counts = torch.bincount(idx.reshape(-1).long(), minlength=E)
+    # When one step's touched weights would fit in L2 (decode shapes), the
+    # steps rotate over ROT_LAYERS distinct seeded layers, as a model's layer
+    # loop does: each step's weights were last read ROT_LAYERS - 1 steps (far
+    # more than L2's worth of other weights) earlier, so they come from HBM,
+    # while the kernels' code and the tokens stay cached.
+    rotate = distinct * expert_bytes(shape) < 2 * L2_BYTES
+    layers = [p] + ([make_layer(shape, 1000 + 10 * case_id + i, device=dev) for i in range(1, ROT_LAYERS)]
+                    if rotate else [])
+    calls = [layer] + [layer_fn(lp) for lp in layers[1:]]
+    distincts = [distinct]
+    for c in calls[1:]:
+        _, _, idx_r = c(x)
+        distincts.append(int(torch.unique(idx_r).numel()))
+    torch.cuda.synchronize()
     graphed = not args.no_graph
     graph_ok = None
     if graphed:
         # the whole layer (no host synchronization inside) replayed from a CUDA graph
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            g_out, _, _ = layer(x)
-        graph.replay()
-        torch.cuda.synchronize()
-        graph_ok = bool(torch.equal(g_out, out))
-        step = graph.replay
-    distinct = int(torch.unique(idx).numel())
-    counts = torch.bincount(idx.reshape(-1).long(), minlength=E)
+        graphs = []
+        for i, c in enumerate(calls):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                g_out, _, _ = c(x)
+            g.replay()
+            torch.cuda.synchronize()
+            if i == 0:
+                graph_ok = bool(torch.equal(g_out, out))
+            graphs.append(g)
+        replays = [g.replay for g in graphs]
+    else:
+        replays = [(lambda c=c: c(x)) for c in calls]
+    turn = [0]
+
+    def step():
+        replays[turn[0] % len(replays)]()
+        turn[0] += 1
     assert kernels.device_status(clear=True) == 0
 
-    flush_l2 = distinct * expert_bytes(shape) < 2 * L2_BYTES
-    flush_buf = torch.empty(2 * L2_BYTES, dtype=torch.uint8, device=dev) if flush_l2 else None
     with ClockSampler(local) as clk:
-        ms = time_steps(step, args.steps, flush_buf, world)
+        ms = time_steps(step, args.steps, None, world)
     value = T / (ms * 1e-3)
-    del flush_buf
+    distinct_mean = statistics.mean(distincts)
 
     # per-stage breakdown: each C-ABI stage from its own graph replay.  The
     # decode paths' launches sit inside one C call; their breakdown comes
@@ -563,18 +593,24 @@ def measure(workload, args, world, local):
         del bufs
 
     pipelined = T > 64
-    ms_e2e = e2e_ms(lambda xin: layer(xin, None)[0], x, args.steps, args.warmup, world, pipelined)
+    e2e_turn = [0]
+
+    def e2e_call(xin):
+        c = calls[e2e_turn[0] % len(calls)]
+        e2e_turn[0] += 1
+        return c(xin, None)[0]
+    ms_e2e = e2e_ms(e2e_call, x, args.steps, args.warmup, world, pipelined)
 
     # --- roofline of the dominant kernel
     peaks, peak_src = load_peaks()
     S = T * k
     stage_flops = {"gate_up": S * 4.0 * H * I, "down": S * 2.0 * H * I, "router": 2.0 * T * H * E}
     G = H // 32
-    gu_bytes = distinct * (2 * I * G * 17 + 2 * I * 2) + S * H * 2 + S * I * 2
-    dn_bytes = distinct * (H * (I // 32) * 17 + H * 2) + S * I * 2 + S * H * 2
+    gu_bytes = distinct_mean * (2 * I * G * 17 + 2 * I * 2) + S * H * 2 + S * I * 2
+    dn_bytes = distinct_mean * (H * (I // 32) * 17 + H * 2) + S * I * 2 + S * H * 2
     stage_bytes = {"gate_up": gu_bytes, "down": dn_bytes, "router": E * H * 4 + T * H * 2,
                    "dispatch": 2 * S * H * 2, "combine": S * H * 2 + T * H * 2,
-                   "layer": algorithmic_bytes(T, shape, distinct)}
+                   "layer": algorithmic_bytes(T, shape, distinct_mean)}
     dom = max(stage_ms, key=stage_ms.get)
     tensor_bound = (S / max(distinct, 1)) > 64 and dom in ("gate_up", "down")
     dur_s = stage_ms[dom] * 1e-3
@@ -601,10 +637,10 @@ def measure(workload, args, world, local):
                               "device-timed step; a lower bound for the expert streaming, >97% of the bytes")
     roof["algorithmic"] = {"flops": stage_flops.get(dom), "bytes": stage_bytes.get(dom), "launch_ms": stage_ms[dom]}
     layer_flops = algorithmic_flops(T, shape)
-    layer_bytes = algorithmic_bytes(T, shape, distinct)
+    layer_bytes = algorithmic_bytes(T, shape, distinct_mean)
     t_fp4 = layer_flops / (FP4_DENSE_NOMINAL_TFLOPS * 1e12)
     t_hbm = layer_bytes / (peaks["hbm_gbs"] * 1e9)
-    layer_roof = {"flops": layer_flops, "bytes": layer_bytes, "distinct_experts": distinct,
+    layer_roof = {"flops": layer_flops, "bytes": layer_bytes, "distinct_experts": distinct_mean,
                   "floor_us_fp4_nominal": t_fp4 * 1e6, "floor_us_hbm_measured": t_hbm * 1e6,
                   "frac_of_fp4_hbm_roofline": max(t_fp4, t_hbm) / (ms * 1e-3),
                   "frac_of_bf16_burst_measured": (layer_flops / (ms * 1e-3) / 1e12) / peaks["bf16_tflops"],
@@ -619,8 +655,12 @@ def measure(workload, args, world, local):
                        "weights": "MXFP4 e2m1 + e8m0 scales (uniform codes, scales U{%d..%d})" % (
                            shape.scale_lo, shape.scale_hi),
                        "algo": args.algo, "cuda_graph": graphed, "graph_output_equals_eager": graph_ok,
-                       "l2": ("L2 flushed (256 MB write) before each timed step; steps timed individually"
-                              if flush_l2 else "inputs larger than L2 (expert weights read per step exceed L2)"),
+                       "l2": (f"steps rotate over {len(calls)} distinct seeded layers ({len(calls)} x "
+                              f"{expert_bytes(shape) * E / 1e9:.2f} GB of weights); each step's touched weights "
+                              f"(~{distinct_mean * expert_bytes(shape) / 1e6:.0f} MB) were last read {len(calls) - 1} "
+                              "steps earlier, after more than L2 of other weights, so they come from HBM; the "
+                              "kernels' code and the tokens stay cached, as in a model's layer loop"
+                              if rotate else "inputs larger than L2 (expert weights read per step exceed L2)"),
                        "expert_rows_min_max": [int(counts.min()), int(counts.max())]},
             "roofline": roof, "layer_roofline": layer_roof,
             "e2e": {"value": T / (ms_e2e * 1e-3), "unit": "tokens/s",

@@ -229,11 +229,10 @@ int moe_forward_impl(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, 
   BS_ARG(workspace, "bs_moe_forward: null workspace");
   BS_ALIGNED16(workspace, "workspace");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  // AUTO takes the single-launch decode kernel wherever it applies (T <= 8)
-  const bool fused = algo == BS_ALGO_FUSED ||
-                     (algo == BS_ALGO_AUTO && fused_supported(T, H, I, E, k, alpha, limit, gate_up_blocks,
-                                                              gate_up_scales, down_blocks, down_scales));
-  if (fused) {
+  // the single-launch decode kernel runs on request only: measured with the
+  // weights cold and the code cached (a model's layer loop), the four-launch
+  // block-scaled path below is faster at every T it takes
+  if (algo == BS_ALGO_FUSED) {
     BS_ARG(router_dtype == BS_F32 || router_dtype == BS_BF16 || !router_weight,
            "bs_moe_forward: router dtype must be bf16 or f32");
     BS_ARG(bias_dtype == BS_BF16 || bias_dtype == BS_F32, "bs_moe_forward: bias dtype must be bf16 or f32");
@@ -321,13 +320,10 @@ extern "C" int bs_moe_decode(const void* x, int64_t T, int64_t H, int64_t I, int
                              const void* down_blocks, const void* down_scales, const void* down_bias,
                              int bias_dtype, float alpha, float limit, void* out, void* workspace,
                              size_t workspace_bytes, void* stream) {
-  const int algo = bs::fused_supported(T, H, I, E, k, alpha, limit, gate_up_blocks, gate_up_scales, down_blocks,
-                                       down_scales)
-                       ? BS_ALGO_FUSED
-                       : BS_ALGO_MX;
   return bs::moe_forward_impl(x, T, H, I, E, k, router_weight, router_bias, router_dtype, scores, indices,
                               gate_up_blocks, gate_up_scales, gate_up_bias, down_blocks, down_scales, down_bias,
-                              bias_dtype, alpha, limit, out, workspace, workspace_bytes, algo, stream, nullptr);
+                              bias_dtype, alpha, limit, out, workspace, workspace_bytes, BS_ALGO_MX, stream,
+                              nullptr);
 }
 
 extern "C" size_t bs_moe_block_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t k) {

@@ -51,8 +51,8 @@ enum bs_algo {
   BS_ALGO_TCGEN05 = 2,  /* tcgen05/TMEM grouped GEMM (prefill shapes)                 */
   BS_ALGO_MX = 3,       /* bs_moe_forward only, T <= 64: tcgen05 block-scaled MMAs on  */
                         /* the e2m1 codes (activations as four e2m1 terms)            */
-  BS_ALGO_FUSED = 4     /* bs_moe_forward only, T <= 8: the whole layer in ONE         */
-                        /* cooperative persistent kernel (what AUTO picks there)      */
+  BS_ALGO_FUSED = 4     /* bs_moe_forward only, T <= 8, on request: the whole layer in */
+                        /* ONE cooperative persistent kernel                           */
 };
 
 /* Library identity. */
@@ -237,14 +237,13 @@ int bs_mxfp4_matmul(const void* x, int64_t m, int64_t K, const void* blocks, con
  *  - router_weight/router_bias non-NULL: computes scores/indices into the
  *    caller's `scores` [T,k] f32 and `indices` [T,k] int32 buffers.
  *  - router_weight NULL: `scores` and `indices` are inputs.
- *  - algo BS_ALGO_FUSED (T <= 8; what BS_ALGO_AUTO picks there when the
- *    shapes allow: H, I multiples of 64 up to 4096, k <= 8, alpha > 0,
- *    limit <= 180, 16-byte aligned weights): router, top-k, dispatch,
- *    gate_up + SwiGLU, down and combine in one cooperative launch with one
- *    CTA per SM, every SM streaming its slice of the routed experts' packed
- *    weights (a 1-D bulk copy per expert run) into shared memory; grid-wide
- *    steps between the phases are bounded waits.
- *  - algo BS_ALGO_MX (T <= 64; what BS_ALGO_AUTO picks for 8 < T <= 64): the
+ *  - algo BS_ALGO_FUSED (T <= 8, only when requested; H, I multiples of 64
+ *    up to 4096, k <= 8, alpha > 0, limit <= 180, 16-byte aligned weights):
+ *    router, top-k, dispatch, gate_up + SwiGLU, down and combine in one
+ *    cooperative launch with one CTA per SM, every SM streaming its slice of
+ *    the routed experts' packed weights (a 1-D bulk copy per expert run) into
+ *    shared memory; grid-wide steps between the phases are bounded waits.
+ *  - algo BS_ALGO_MX (T <= 64; what BS_ALGO_AUTO picks there): the
  *    decode path -- four launches chained with programmatic dependent launch;
  *    the expert projections run on tcgen05 block-scaled MMAs that read the
  *    e2m1 codes and e8m0 scales as stored.
@@ -258,10 +257,11 @@ int bs_moe_forward(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, in
                    int bias_dtype, float alpha, float limit, void* out, void* workspace,
                    size_t workspace_bytes, int algo, void* stream);
 
-/* Decode-shape layer (T <= 64 tokens; H and I multiples of 64; blocks and
- * scales 16-byte aligned): bs_moe_forward restricted to the decode paths --
- * the fused single-launch kernel (BS_ALGO_FUSED) where it applies, else the
- * four-launch block-scaled path (BS_ALGO_MX).  Replaces the same reference lines as bs_moe_forward
+/* Decode-shape layer: bs_moe_forward with BS_ALGO_MX (T <= 64 tokens; H and I
+ * multiples of 64; blocks and scales 16-byte aligned): router, top-k and
+ * dispatch, gate_up + SwiGLU and down on tcgen05 block-scaled MMAs over the
+ * stored e2m1 codes, combine -- four launches chained with programmatic
+ * dependent launch.  Replaces the same reference lines as bs_moe_forward
  * (modeling_gpt_oss.py:140-146 with gptoss.py:137-177) at decode sizes.
  * Workspace: bs_moe_workspace_bytes. */
 int bs_moe_decode(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, int64_t k,

@@ -161,8 +161,8 @@ def test_decode_matches_across_calls_and_graph():
 
 def test_bs_moe_decode_entry_point_matches_forward():
     """bs_moe_decode (the decode-shape C entry point) gives the same bits as
-    bs_moe_forward's AUTO choice (the single-launch kernel at T <= 8, the
-    block-scaled path above), and rejects more than 64 tokens."""
+    bs_moe_forward's AUTO choice (the block-scaled path at T <= 64), and
+    rejects more than 64 tokens."""
     import ctypes
     from blockstreamer_b200 import _lib
     shape = LayerShape(512, 512, 32, 4)

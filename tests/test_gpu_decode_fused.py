@@ -1,4 +1,4 @@
-"""GPU parity of the single-launch decode kernel (BS_ALGO_FUSED, T <= 8).
+"""GPU parity of the single-launch decode kernel (BS_ALGO_FUSED, T <= 8, on request).
 
 Against the reference's golden outputs and the fp32 oracle
 (block_streamer/gptoss.py:137-177, transformers modeling_gpt_oss.py:126-146):
@@ -167,8 +167,6 @@ def test_fused_deterministic_across_calls_and_graph():
     a = kernels.moe_forward(*args, **kw)[0].clone()
     b = kernels.moe_forward(*args, **kw)[0].clone()
     assert torch.equal(a, b)
-    auto = kernels.moe_forward(*args, router_weight=p["router.weight"], router_bias=p["router.bias"])[0]
-    assert torch.equal(a, auto)                      # AUTO picks this path at T <= 8
     ws = torch.empty(1 << 24, dtype=torch.uint8, device=DEV)
     s = torch.cuda.Stream()
     s.wait_stream(torch.cuda.current_stream())

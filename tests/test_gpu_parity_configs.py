@@ -5,9 +5,9 @@
   the 320-row tile with its second 128 x 64 MMA or a two-chunk split);
 * gpt-oss-20b prefill, 4096 tokens, 32 experts (config 2: ~512 rows per
   expert, several token chunks per expert);
-* gpt-oss-120b decode, 1 / 8 / 64 tokens (config 3: the single-launch decode
-  kernel at 1 and 8 tokens, the block-scaled decode path at all three, with
-  gathered activation rows above 16 tokens).
+* gpt-oss-120b decode, 1 / 8 / 64 tokens (config 3: the block-scaled decode
+  path at all three, with gathered activation rows above 16 tokens, and the
+  single-launch kernel at 1 and 8 tokens).
 
 Each test runs the layer through the C ABI (``bs_moe_forward``, router
 included) and checks, following block_streamer/gptoss.py:137-177 and
@@ -145,21 +145,20 @@ def test_decode_parity_at_bench_config(T):
     args = layer_args(p)
     out, sc, idx = kernels.moe_forward(x, *args, k, router_weight=p["router.weight"],
                                        router_bias=p["router.bias"], algo=kernels.ALGO_AUTO)
-    # AUTO: the single-launch kernel at T <= 8, the block-scaled path above
-    algo = kernels.ALGO_FUSED if T <= 8 else kernels.ALGO_MX
+    # AUTO takes the block-scaled decode path at T <= 64
     out_a, sc_a, idx_a = kernels.moe_forward(x, *args, k, router_weight=p["router.weight"],
-                                             router_bias=p["router.bias"], algo=algo)
+                                             router_bias=p["router.bias"], algo=kernels.ALGO_MX)
     torch.cuda.synchronize()
     assert torch.equal(out, out_a) and torch.equal(idx, idx_a)
     check_routing(x, p, k, sc, idx)
     print(f"T={T}: {int(torch.unique(idx).numel())} distinct experts")
     ref = omoe.experts_fp32(x, idx.long(), sc, experts_of(p))
     check_close(out, ref, f"120b decode T={T} layer")
-    if T <= 8:   # the four-launch block-scaled path on the same inputs
-        out_mx, _, idx_mx = kernels.moe_forward(x, *args, k, router_weight=p["router.weight"],
-                                                router_bias=p["router.bias"], algo=kernels.ALGO_MX)
-        assert torch.equal(idx_mx, idx)
-        check_close(out_mx, ref, f"120b decode T={T} block-scaled path")
+    if T <= 8:   # the single-launch kernel (on request) on the same inputs
+        out_f, _, idx_f = kernels.moe_forward(x, *args, k, router_weight=p["router.weight"],
+                                              router_bias=p["router.bias"], algo=kernels.ALGO_FUSED)
+        assert torch.equal(idx_f, idx)
+        check_close(out_f, ref, f"120b decode T={T} single-launch kernel")
     # against the prefill kernels (tcgen05 grouped GEMM) on the same routing
     out_tc, _, _ = kernels.moe_forward(x, *args, k, indices=idx, scores=sc, algo=kernels.ALGO_TCGEN05)
     check_close(out_tc, ref, f"120b T={T} tcgen05 path")
