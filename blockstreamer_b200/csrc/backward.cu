@@ -6,14 +6,16 @@
 // per-expert loop (host syncs per expert) and multiplies by a densely
 // dequantized weight.  Here, for S = T * k routed rows:
 //   1. dispatch (the forward's grouping) and x_perm;
-//   2. g = x_perm @ W_gu^T + b_gu  (forward grouped GEMM, plain epilogue);
-//   3. h = SwiGLU(g)               (swiglu_rows_kernel, from bf16 g as the
-//      reference's bf16 autograd does);
+//   2. g = x_perm @ W_gu^T + b_gu  (forward grouped GEMM, plain epilogue, fp32:
+//      the clamps of the SwiGLU decide which elements pass a gradient, and
+//      with bf16 g the decisions near +-limit flip against an fp32
+//      evaluation -- at saturating shapes that alone moves dL/dx by ~4%);
+//   3. h = SwiGLU(g)               (swiglu_rows_kernel, bf16 h);
 //   4. y = h @ W_d^T + b_d         (forward grouped GEMM);
 //   5. dw[t,s] = <dout[t], y[row]>, dy[row] = w[t,s] * dout[t]
 //      (combine_backward_kernel: the backward of out = sum_s w * y);
 //   6. dg = SwiGLU'(g) * (dy @ W_d)   (transposed grouped GEMM, SwiGLU-backward
-//      epilogue, in place over g);
+//      epilogue, bf16 dg);
 //   7. dx_perm = dg @ W_gu            (transposed grouped GEMM);
 //   8. dx[t] = sum_s dx_perm[row(t,s)] (unpermute_sum_kernel, fp32).
 // The router's part (GptOssTopKRouter, modeling_gpt_oss.py:126-130: logits,
@@ -40,13 +42,13 @@ int tc_grouped_t_launch(int epi, const void* dy, const int32_t* offsets, int64_t
 namespace {
 
 // h[r, i] = (clamp(up) + 1) * min(gate, L) * sigmoid(alpha * min(gate, L)),
-// gate = g[r, 2i], up = g[r, 2i + 1] (gptoss.py:130-135), in fp32 from bf16 g.
-__global__ void __launch_bounds__(256) swiglu_rows_kernel(const uint32_t* __restrict__ g, int64_t n_pairs,
+// gate = g[r, 2i], up = g[r, 2i + 1] (gptoss.py:130-135), from fp32 g.
+__global__ void __launch_bounds__(256) swiglu_rows_kernel(const float2* __restrict__ g, int64_t n_pairs,
                                                           float alpha, float limit, uint16_t* __restrict__ h) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n_pairs; i += (int64_t)gridDim.x * blockDim.x) {
-    const uint32_t v = g[i];
-    const float gate = fminf(bf16lo(v), limit);
-    const float up = fminf(fmaxf(bf16hi(v), -limit), limit);
+    const float2 v = g[i];
+    const float gate = fminf(v.x, limit);
+    const float up = fminf(fmaxf(v.y, -limit), limit);
     h[i] = __bfloat16_as_ushort(__float2bfloat16_rn((up + 1.0f) * (gate / (1.0f + expf(-alpha * gate)))));
   }
 }
@@ -164,7 +166,8 @@ struct BwdWS {
   int32_t* row_of_slot;
   int32_t* token_of_row;
   uint16_t* xp;   // x_perm, later dy
-  uint16_t* g;    // gate_up pre-activation, later dg (in place)
+  float* g;       // gate_up pre-activation (fp32)
+  uint16_t* dg;   // its gradient
   uint16_t* h;
   uint16_t* y;    // down output, later dx_perm
   uint8_t* scales_t;
@@ -186,7 +189,8 @@ BwdWS bwd_carve(void* base, int64_t T, int64_t H, int64_t I, int64_t E, int64_t 
   w.row_of_slot = reinterpret_cast<int32_t*>(take((size_t)S * 4));
   w.token_of_row = reinterpret_cast<int32_t*>(take((size_t)S * 4));
   w.xp = reinterpret_cast<uint16_t*>(take((size_t)S * H * 2));
-  w.g = reinterpret_cast<uint16_t*>(take((size_t)S * 2 * I * 2));
+  w.g = reinterpret_cast<float*>(take((size_t)S * 2 * I * 4));
+  w.dg = reinterpret_cast<uint16_t*>(take((size_t)S * 2 * I * 2));
   w.h = reinterpret_cast<uint16_t*>(take((size_t)S * I * 2));
   w.y = reinterpret_cast<uint16_t*>(take((size_t)S * H * 2));
   w.scales_t = reinterpret_cast<uint8_t*>(take(std::max(tc_t_scales_bytes(E, H, I), tc_t_scales_bytes(E, 2 * I, H))));
@@ -244,9 +248,9 @@ extern "C" int bs_moe_backward(const void* x, int64_t T, int64_t H, int64_t I, i
   // 1-4: the forward's intermediates, recomputed
   BS_TRY(dispatch_launch(indices, BS_I32, T, k, E, x, H, w.offsets, w.row_of_slot, w.token_of_row, w.xp, w.dispatch,
                          w.dispatch_bytes, st));
-  BS_TRY(tc_grouped_launch(1, w.xp, w.offsets, S, S, E, H, 2 * I, gate_up_blocks, gate_up_scales, gate_up_bias, bf32,
+  BS_TRY(tc_grouped_launch(2, w.xp, w.offsets, S, S, E, H, 2 * I, gate_up_blocks, gate_up_scales, gate_up_bias, bf32,
                            0.f, 0.f, w.g, st));
-  swiglu_rows_kernel<<<grid_for(S * I), 256, 0, st>>>(reinterpret_cast<const uint32_t*>(w.g), S * I, alpha, limit,
+  swiglu_rows_kernel<<<grid_for(S * I), 256, 0, st>>>(reinterpret_cast<const float2*>(w.g), S * I, alpha, limit,
                                                       w.h);
   BS_LAUNCHED();
   BS_TRY(tc_grouped_launch(1, w.h, w.offsets, S, S, E, I, H, down_blocks, down_scales, down_bias, bf32, 0.f, 0.f,
@@ -261,11 +265,11 @@ extern "C" int bs_moe_backward(const void* x, int64_t T, int64_t H, int64_t I, i
                                                              w.row_of_slot, weights, T, (int)k, (int)H, grad_weights,
                                                              w.xp);
   BS_LAUNCHED();
-  // 6: dg = SwiGLU'(g) * (dy @ W_d), in place over g
+  // 6: dg = SwiGLU'(g) * (dy @ W_d)
   BS_TRY(tc_grouped_t_launch(1, w.xp, w.offsets, S, E, H, I, down_blocks, down_scales, w.scales_t, w.g, alpha, limit,
-                             w.g, st));
+                             w.dg, st));
   // 7: dx_perm = dg @ W_gu (into the y buffer)
-  BS_TRY(tc_grouped_t_launch(0, w.g, w.offsets, S, E, 2 * I, H, gate_up_blocks, gate_up_scales, w.scales_t, nullptr,
+  BS_TRY(tc_grouped_t_launch(0, w.dg, w.offsets, S, E, 2 * I, H, gate_up_blocks, gate_up_scales, w.scales_t, nullptr,
                              0.f, 0.f, w.y, st));
   // 8: dx[t] = sum over the token's slots
   unpermute_sum_kernel<<<grid_for(T * H / 2), 256, 0, st>>>(reinterpret_cast<const uint32_t*>(w.y), w.row_of_slot, T,

@@ -26,6 +26,8 @@
 // clean exit, TMEM freed).
 // MODE 0: gate_up — bias + clamped interleaved SwiGLU (gptoss.py:130-135,158-166).
 // MODE 1: plain   — bias (gptoss.py:167-174) / mxfp4_matmul.
+// MODE 2: plain   — bias, fp32 output (the backward's recomputed gate_up
+//                   pre-activation, whose clamp masks must match fp32).
 #include <cudaTypedefs.h>
 
 #include "bs_common.cuh"
@@ -133,7 +135,7 @@ __device__ __forceinline__ float swiglu_fast(float gate, float up, float alpha, 
 
 // One 16-column chunk of the accumulator (one token per column) for the lane's
 // weight row: bias, then SwiGLU across the (gate, up) lane pair (MODE 0) or the
-// plain projection (MODE 1), stored as bf16.
+// plain projection (MODE 1: bf16; MODE 2: fp32).
 template <int MODE>
 __device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[16], int c0, const Tile& t, int row_w,
                                                bool rv, float bv, float bp, int lane, int Nw,
@@ -157,13 +159,20 @@ __device__ __forceinline__ void epilogue_chunk(const uint32_t (&v)[16], int c0, 
       const int n = c0 + 2 * jj + odd;
       if (n < t.nrows && rv) orow[(t.r0 + n) * Iout] = __bfloat16_as_ushort(__float2bfloat16_rn(hv));
     }
-  } else {
+  } else if (MODE == 1) {
     uint16_t* ocol = out + row_w;
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
       const int n = c0 + i;
       if (n < t.nrows && rv)
         ocol[(t.r0 + n) * Nw] = __bfloat16_as_ushort(__float2bfloat16_rn(__uint_as_float(v[i]) + bv));
+    }
+  } else {
+    float* ocol = reinterpret_cast<float*>(out) + row_w;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int n = c0 + i;
+      if (n < t.nrows && rv) ocol[(t.r0 + n) * Nw] = __uint_as_float(v[i]) + bv;
     }
   }
 }
@@ -466,7 +475,7 @@ int tc_grouped_launch(int mode, const void* x, const int32_t* offsets, int64_t r
   const size_t smem = 1024 + (size_t)kStagesB * kBBytes + (size_t)kStagesA * kABytes + 2 * scale_buf +
                       kNumBars * 8 + 16 + (size_t)2 * (E + 1) * sizeof(int);
   BS_REQUIRE(smem <= 227 * 1024, BS_ERR_CAPACITY, "tcgen05 GEMM: too many experts for shared memory");
-  auto kern = mode == 0 ? tc_grouped_kernel<0> : tc_grouped_kernel<1>;
+  auto kern = mode == 0 ? tc_grouped_kernel<0> : mode == 1 ? tc_grouped_kernel<1> : tc_grouped_kernel<2>;
   BS_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   const int grid = sm_count();
   kern<<<grid, kThreads, smem, st>>>(tm_b, tm_a, static_cast<const uint8_t*>(scales), offsets,

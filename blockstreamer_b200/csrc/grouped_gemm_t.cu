@@ -24,10 +24,10 @@
 //   * D: fp32 accumulators in TMEM, drained by four epilogue warps.
 // EPI 0: plain bf16 store (dx of the gate_up projection, mxfp4_matmul's dx).
 // EPI 1: the SwiGLU backward of gptoss.py:130-135 fused in: the accumulator is
-//   dh for intermediate feature i; with the saved gate_up pre-activation g it
-//   writes dg[:, 2i] (gate) and dg[:, 2i+1] (up) -- the gradient the gate_up
-//   backward consumes (in place over g is allowed: each pair is read, then
-//   written, by the same thread).
+//   dh for intermediate feature i; with the gate_up pre-activation g (fp32,
+//   so that the clamp masks match an fp32 evaluation) it writes dg[:, 2i]
+//   (gate) and dg[:, 2i+1] (up) in bf16 -- the gradient the gate_up backward
+//   consumes.
 // Every wait is bounded (timeout -> status word + clean exit, TMEM freed).
 // No TMA multicast.
 #include <cudaTypedefs.h>
@@ -165,7 +165,7 @@ template <int EPI>
 __global__ void __launch_bounds__(kThreads, 1) tc_grouped_t_kernel(
     const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_a,
     const __grid_constant__ CUtensorMap tm_s, const int* __restrict__ offsets, int64_t rows_total, int E,
-    int Nw, int Kw, int Gp, const uint16_t* __restrict__ g, float alpha, float limit, uint16_t* __restrict__ out,
+    int Nw, int Kw, int Gp, const float* __restrict__ g, float alpha, float limit, uint16_t* __restrict__ out,
     int* status) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -346,9 +346,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_t_kernel(
           if (EPI == 0) {
             out[row * Kw + feat] = __bfloat16_as_ushort(__float2bfloat16_rn(acc));
           } else {
-            const uint32_t gp = *reinterpret_cast<const uint32_t*>(g + row * 2 * Kw + 2 * feat);
+            const float2 gp = *reinterpret_cast<const float2*>(g + row * 2 * Kw + 2 * feat);
             float dgate, dup;
-            swiglu_backward(bf16lo(gp), bf16hi(gp), acc, alpha, limit, dgate, dup);
+            swiglu_backward(gp.x, gp.y, acc, alpha, limit, dgate, dup);
             *reinterpret_cast<uint32_t*>(out + row * 2 * Kw + 2 * feat) = pack_bf16x2(dgate, dup);
           }
         }
@@ -456,7 +456,8 @@ size_t tc_t_scales_bytes(int64_t E, int64_t Nw, int64_t Kw) {
 bool tc_t_supported(int64_t Nw, int64_t Kw) { return Nw % 64 == 0 && Kw % 32 == 0 && Kw / 32 <= 1024; }
 
 // dx[rows, Kw] = dy[rows, Nw] @ dequant(W[e]) per expert segment (epi 0), or
-// with the SwiGLU backward fused (epi 1: Kw = I, g/out [rows, 2I]).
+// with the SwiGLU backward fused (epi 1: Kw = I, g [rows, 2I] fp32, out
+// [rows, 2I] bf16).
 // `scales_t` is a workspace of tc_t_scales_bytes; it is rebuilt from `scales`.
 int tc_grouped_t_launch(int epi, const void* dy, const int32_t* offsets, int64_t rows_total, int64_t E, int64_t Nw,
                         int64_t Kw, const void* blocks, const void* scales, void* scales_t, const void* g,
@@ -490,7 +491,7 @@ int tc_grouped_t_launch(int epi, const void* dy, const int32_t* offsets, int64_t
   auto kern = epi == 0 ? tc_grouped_t_kernel<0> : tc_grouped_t_kernel<1>;
   BS_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   kern<<<sm_count(), kThreads, smem, st>>>(tm_b, tm_a, tm_s, offsets, rows_total, (int)E, (int)Nw, (int)Kw, (int)Gp,
-                                           static_cast<const uint16_t*>(g), alpha, limit,
+                                           static_cast<const float*>(g), alpha, limit,
                                            static_cast<uint16_t*>(out), device_status_ptr());
   BS_LAUNCHED();
   return BS_OK;

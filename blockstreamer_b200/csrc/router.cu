@@ -148,6 +148,11 @@ __global__ void __launch_bounds__(256) router_logits_small_kernel(
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
   const int lane = threadIdx.x & 31;
   if (warp >= E) return;
+  // blockIdx.y: this CTA's chunk of MaxT tokens
+  const int t0 = blockIdx.y * MaxT;
+  x += (int64_t)t0 * H;
+  logits += (int64_t)t0 * E;
+  T = min(T - t0, MaxT);
   const WT* w = W + (int64_t)warp * H;
   float acc[MaxT];
 #pragma unroll
@@ -206,8 +211,10 @@ int launch_router(const void* x, const void* w, const void* b, int T, int H, int
   const XT* xp = static_cast<const XT*>(x);
   const WT* wp = static_cast<const WT*>(w);
   const WT* bp = static_cast<const WT*>(b);
-  if (logits && T <= 8) {
-    const int grid = (int)cdiv(E, 8);
+  if (logits && T <= 64) {
+    // one warp per (expert, 8 tokens): E/8 x T/8 CTAs, so that even a few
+    // tokens spread over the SMs
+    const dim3 grid((unsigned)cdiv(E, 8), (unsigned)cdiv(T, 8));
     router_logits_small_kernel<XT, WT, 8><<<grid, 256, 0, st>>>(xp, wp, bp, T, H, E, bf16_logits, logits);
     BS_LAUNCHED();
     router_topk_kernel<<<(unsigned)cdiv(T, 8), 256, 0, st>>>(logits, T, E, k, scores, i32, i64);

@@ -15,8 +15,8 @@
 //     corrections — which the epilogue warps drain into fp32 registers while
 //     the MMA fills the other pair (double buffered).  Measured logit error is
 //     then below the reference's own CPU fp32 GEMM.
-//   * Parallelism: a token tile of 128 is split over K across up to 4 CTAs so
-//     the grid fills the SMs; each CTA writes fp32 partial logits and a
+//   * Parallelism: a token tile of 128 is split over K across up to 16 CTAs
+//     so the grid fills the SMs at any token count; each CTA writes fp32 partial logits and a
 //     warp-per-token kernel (router.cu) adds the partials and the bias, then
 //     runs top-k (ties go to the lower expert index) and the softmax.
 #include "bs_common.cuh"
@@ -210,10 +210,19 @@ __global__ void __launch_bounds__(kRThreads, 1) router_tc_kernel(
 
 int64_t padded_experts(int64_t E) { return (E + 15) / 16 * 16; }
 
-// K splits per token tile, so that the grid fills the SMs.
-int router_splits(int64_t T) {
-  const int64_t tiles = cdiv(T, kRBM);
-  return (int)std::max<int64_t>(1, std::min<int64_t>(4, sm_count() / std::max<int64_t>(tiles, 1)));
+// K splits per token tile, so that the grid fills the SMs even with few
+// token tiles (an expert-parallel rank routes T / R tokens): up to 16, each
+// split keeping at least two K steps.  split_cap bounds it independently of
+// the device, for the workspace size.
+constexpr int kMaxSplits = 16;
+int64_t split_cap(int64_t T) {
+  const int64_t tiles = std::max<int64_t>(cdiv(T, kRBM), 1);
+  return std::max<int64_t>(1, std::min<int64_t>(kMaxSplits, 256 / tiles));
+}
+int router_splits(int64_t T, int64_t H) {
+  const int64_t tiles = std::max<int64_t>(cdiv(T, kRBM), 1);
+  const int64_t ks = cdiv(H, kRBK);
+  return (int)std::max<int64_t>(1, std::min<int64_t>(std::min<int64_t>(split_cap(T), ks / 2), sm_count() / tiles));
 }
 
 }  // namespace
@@ -226,7 +235,8 @@ int router_finish_launch(const float* partial, int ns, int64_t T, int64_t Ep, in
 size_t router_tc_workspace_bytes(int64_t T, int64_t H, int64_t E, int w_dtype) {
   const int nterms = w_dtype == BS_F32 ? 3 : 1;
   const int64_t Ep = padded_experts(E);
-  return align_up((size_t)nterms * Ep * H * 2, 256) + align_up((size_t)4 * std::max<int64_t>(T, 1) * Ep * 4, 256);
+  return align_up((size_t)nterms * Ep * H * 2, 256) +
+         align_up((size_t)split_cap(T) * std::max<int64_t>(T, 1) * Ep * 4, 256);
 }
 
 bool router_tc_supported(int x_dtype, int64_t T, int64_t H, int64_t E, int64_t k, const void* x) {
@@ -267,7 +277,7 @@ int router_tc_launch(const void* x, const void* weight, const void* bias, int w_
   while (cols < (uint32_t)(2 * (nterms == 3 ? 2 : 1) * Ep)) cols <<= 1;
   auto kern = nterms == 3 ? router_tc_kernel<3> : router_tc_kernel<1>;
   BS_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  const int ns = router_splits(T);
+  const int ns = router_splits(T, H);
   dim3 grid((unsigned)cdiv(T, kRBM), (unsigned)ns);
   kern<<<grid, kRThreads, smem, st>>>(tm_x, tm_w, (int)T, (int)H, (int)Ep, stages, cols, partial,
                                       device_status_ptr());
