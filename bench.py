@@ -673,6 +673,45 @@ def measure(workload, args, world, local):
             "gpu_launches": (1 if fused_path else 4 if mx_path else sum(LAUNCHES.values())) * args.steps}
 
 
+def measure_backward(args, local):
+    """The expert layer's backward (bs_moe_backward: dL/dx and dL/d routing
+    weights) at the default workload, graph-replayed and device-timed: the
+    forward's dispatch and projections recomputed, two transposed grouped
+    GEMMs, the weighted-sum and un-permute backward."""
+    key, case_id, T = parse_workload(DEFAULT_WORKLOAD)
+    shape = CASES[key]
+    k, E, H, I = shape.top_k, shape.experts, shape.hidden, shape.intermediate
+    dev = torch.device("cuda", torch.cuda.current_device())
+    p = make_layer(shape, case_id, device=dev)
+    x = make_tokens(T, H, case_id, device=dev)
+    _, sc, idx = kernels.router(x, p["router.weight"], p["router.bias"], k, index_dtype=torch.int32)
+    gout = torch.randn(T, H, generator=torch.Generator(device=dev).manual_seed(9), device=dev).to(torch.bfloat16)
+    names = ("gate_up_proj_blocks", "gate_up_proj_scales", "gate_up_proj_bias", "down_proj_blocks",
+             "down_proj_scales", "down_proj_bias")
+    pe = [p["experts." + n] for n in names]
+    for _ in range(args.warmup):
+        kernels.moe_backward(x, idx, sc, gout, *pe)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        kernels.moe_backward(x, idx, sc, gout, *pe)
+    g.replay()
+    torch.cuda.synchronize()
+    assert kernels.device_status(clear=True) == 0
+    ms = time_steps(g.replay, args.steps, None, 1)
+    S = T * k
+    # recomputed forward projections (2 * S * H * 3I) + the two transposed GEMMs (same FLOPs)
+    flops = 2.0 * (S * 2.0 * H * 3 * I)
+    peaks, peak_src = load_peaks()
+    peak, plabel = tensor_peak(peaks, ms * args.steps * 1e-3)
+    return {"value": T / (ms * 1e-3), "unit": "tokens/s", "ms_per_step": ms,
+            "what": "bs_moe_backward: dL/dx and dL/d routing weights of the expert layer (recomputed forward "
+                    "projections, transposed tcgen05 GEMMs for dh and dx), CUDA-graph replay",
+            "roofline": {"bound": "tensor", "achieved": flops / (ms * 1e-3) / 1e12, "peak": peak,
+                         "unit": "TFLOP/s", "frac": flops / (ms * 1e-3) / 1e12 / peak,
+                         "peak_source": f"{peak_src} {plabel}", "flops_per_step": flops}}
+
+
 def run_ours(args, rank, world, local):
     key, case_id, T_total = parse_workload(args.workload)
     shape = CASES[key]
@@ -691,6 +730,8 @@ def run_ours(args, rank, world, local):
             extra[w] = {n: r[n] for n in ("value", "unit", "ms_per_step", "roofline", "layer_roofline", "e2e",
                                           "clocks", "gpu_launches")}
             extra[w]["config"] = r["config"]
+        extra["gptoss120b-prefill-8192-backward"] = measure_backward(args, local)
+        torch.cuda.empty_cache()
         line["configs"] = extra
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         shape_c, p_c, x_c = cpu_inputs(key, case_id, T_total)

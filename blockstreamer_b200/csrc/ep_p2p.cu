@@ -109,6 +109,22 @@ __device__ __forceinline__ T* at(uint64_t base, size_t off) {
   return reinterpret_cast<T*>(base + off);
 }
 
+// One warp copies a row of `vecs` 16-byte words (src local, dst possibly a
+// peer's memory): four loads in flight per lane before its stores, so the
+// row's load latency is paid once per four words rather than per word.
+__device__ __forceinline__ void copy_row(uint4* __restrict__ dst, const uint4* __restrict__ src, int64_t vecs,
+                                         int lane) {
+  int64_t v = lane;
+  for (; v + 96 < vecs; v += 128) {
+    const uint4 a = src[v], b = src[v + 32], c = src[v + 64], d = src[v + 96];
+    dst[v] = a;
+    dst[v + 32] = b;
+    dst[v + 64] = c;
+    dst[v + 96] = d;
+  }
+  for (; v < vecs; v += 32) dst[v] = src[v];
+}
+
 // Last index i in [0, n) with a[i] <= v (a ascending, a[0] <= v).
 __device__ __forceinline__ int last_le(const int* a, int n, int v) {
   int lo = 0, hi = n - 1;
@@ -196,7 +212,7 @@ __global__ void __launch_bounds__(256) ep_scatter_kernel(const uint4* __restrict
     }
     const uint4* src = x + (int64_t)token_of_row[r] * vecs;
     uint4* dst = at<uint4>(bases[d], L.recv) + dst_row * vecs;
-    for (int64_t v = lane; v < vecs; v += 32) dst[v] = src[v];
+    copy_row(dst, src, vecs, lane);
   }
   __threadfence_system();
   __syncthreads();
@@ -282,7 +298,7 @@ __global__ void __launch_bounds__(256) ep_return_kernel(const uint4* __restrict_
     }
     const uint4* a = y + (int64_t)r * vecs;
     uint4* b = at<uint4>(bases[s], L.yback) + dst_row * vecs;
-    for (int64_t v = lane; v < vecs; v += 32) b[v] = a[v];
+    copy_row(b, a, vecs, lane);
   }
   __threadfence_system();
   __syncthreads();
