@@ -878,122 +878,271 @@ def run_bench_ep(args, rank, world, local, shape, case_id, T_total):
 
 # ---------------------------------------------------------------- streamed stack (config 5)
 
-def run_bench_streamed(args, rank, world, shape, case_id, T, layers=4, zipf_s=1.2):
-    """Config 5: a stack of ``layers`` B200GptOssMLP blocks whose expert
-    weights live in pinned host memory and stream into HBM through the
-    reference's own StreamedModel (prefetch_ahead=1, functional_call binding),
-    T tokens, router bias making expert popularity Zipf(s) over a seeded
-    expert permutation.  value = T * layers / step time (tokens through one
-    MoE layer per second); the host->device link bounds it."""
+def run_bench_streamed(args, rank, world, shape, case_id, T, layers=4, zipf_s=1.2, groups=4):
+    """Config 5: a stack of ``layers`` gpt-oss-120b MoE layers whose packed
+    experts live in pinned host memory, T tokens in total, router bias making
+    expert popularity Zipf(s) over a seeded expert permutation.
+
+    value = T * layers / step time (tokens through one MoE layer per second,
+    whole job).  The engine is blockstreamer_b200.streaming: per layer the
+    router runs on resident router weights, only the experts that received
+    rows are staged host->device, in ``groups`` id ranges whose grouped GEMMs
+    start as each range lands.  At N > 1 every rank keeps only its E/N-expert
+    slice of each layer pinned, routes T/N tokens and exchanges rows over peer
+    memory (StreamedEPStack).  At N = 1 the reference's own StreamedModel
+    (whole-block staging, prefetch_ahead=1) drives the same layers as
+    B200GptOssMLP blocks for comparison.  After timing, every rank checks its
+    output against the resident layers chained on the same tokens."""
     import types
-    if world > 1:
-        raise SystemExit("the streamed workload runs on one GPU")
-    ref_dir = os.path.join(REPO, "baseline", "_ref")
-    if not os.path.exists(os.path.join(ref_dir, "streamer.py")):
-        raise SystemExit("the streamed workload needs the reference package under baseline/_ref")
-    sys.path.insert(0, ref_dir)
-    from streamer import StreamedModel  # the reference's own streaming engine
+    import torch.distributed as dist
     from blockstreamer_b200 import B200GptOssMLP
+    from blockstreamer_b200.streaming import EXPERT_TENSORS, StreamedEPStack, StreamedMoEStack
     from blockstreamer_b200.synthetic import zipf_router_bias
 
     dev = torch.device("cuda", torch.cuda.current_device())
-    cfg = types.SimpleNamespace(hidden_size=shape.hidden, intermediate_size=shape.intermediate,
-                                num_local_experts=shape.experts, num_experts_per_tok=shape.top_k,
-                                swiglu_limit=7.0)
-    blocks = []
-    for layer in range(layers):
-        p = make_layer(shape, 10 * case_id + layer, device=dev)
-        p["router.bias"] = zipf_router_bias(shape, zipf_s, 10 * case_id + layer).to(dev)
-        mlp = B200GptOssMLP(cfg)
-        mlp.load_state_dict({n: t.cpu() for n, t in p.items()}, strict=True, assign=True)
-        blocks.append(mlp)
+    if T % world or shape.experts % world:
+        raise SystemExit(f"{T} tokens / {shape.experts} experts do not split over {world} ranks")
+    Tr = T // world
+    El = shape.experts // world
+    lo, hi = rank * El, (rank + 1) * El
+
+    def layer_state(li, device):
+        p = make_layer(shape, 10 * case_id + li, device=device)
+        p["router.bias"] = zipf_router_bias(shape, zipf_s, 10 * case_id + li).to(device)
+        return p
+
+    # this rank's slice of every layer in pinned host memory
+    states = []
+    for li in range(layers):
+        p = layer_state(li, dev)
+        states.append({n: (t[lo:hi] if n.startswith("experts.") else t).cpu().pin_memory()
+                       for n, t in p.items()})
         del p
     torch.cuda.empty_cache()
-    x = make_tokens(T, shape.hidden, case_id, device=dev).view(1, T, shape.hidden)
-    hist = torch.bincount(kernels.router(x.view(T, -1), blocks[0].router.weight.to(dev),
-                                         blocks[0].router.bias.to(dev), shape.top_k)[2].reshape(-1).long(),
-                          minlength=shape.experts).cpu()
-    model = StreamedModel(blocks, device=dev, prefetch_ahead=1, dtype=None)
+    x_all = make_tokens(T, shape.hidden, case_id, device=dev)
+    x = x_all[rank * Tr:(rank + 1) * Tr].contiguous()
+    del x_all
+    exchange = None
+    if world == 1:
+        stack = StreamedMoEStack(states, shape.top_k, dev, groups=groups)
+    else:
+        from blockstreamer_b200.expert_parallel import P2PExchange
+        exchange = P2PExchange(None, shape.experts, shape.hidden, Tr, shape.top_k, dev)
+        stack = StreamedEPStack(states, shape.top_k, exchange, groups=groups)
     for _ in range(args.warmup):
-        model(x)
+        stack(x)
     torch.cuda.synchronize()
-    st = torch.cuda.current_stream()
-    b0 = model.stats()["transfer_bytes"]
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n0 = len(stack.stats.bytes_staged)
     with ClockSampler(torch.cuda.current_device()) as clk:
-        torch.cuda.synchronize()
-        ev0.record(st)
-        for _ in range(args.steps):
-            out, _ = model(x)
-        ev1.record(st)
-        torch.cuda.synchronize()
-    ms = ev0.elapsed_time(ev1) / args.steps
-    h2d_per_step = (model.stats()["transfer_bytes"] - b0) / args.steps
-    # the same blocks with every weight resident (compute alone), for the overlap
-    resident = [B200GptOssMLP(cfg) for _ in range(2)]
-    for r, b in zip(resident, blocks[:2]):
-        r.load_state_dict({n: t.to(dev) for n, t in b.state_dict().items()}, strict=True, assign=True)
-    for r in resident:
-        r(x)
+        ms = time_steps(lambda: stack(x), args.steps, None, world)
+    st_bytes = stack.stats.bytes_staged[n0:]
+    st_experts = stack.stats.experts_staged[n0:]
+    st_rows = stack.stats.rows_local[n0:]
+    h2d_per_step = sum(st_bytes) / args.steps            # this rank's weight bytes staged per step
+    out = stack(x)
     torch.cuda.synchronize()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record(st)
-    for _ in range(args.steps):
-        for r in resident:
-            r(x)
-    b.record(st)
+
+    # parity: the resident layers chained on this rank's tokens, single GPU
+    ref = x
+    for li in range(layers):
+        p = layer_state(li, dev)
+        ref, _, _ = kernels.moe_forward(ref, *[p["experts." + n] for n in EXPERT_TENSORS], shape.top_k,
+                                        router_weight=p["router.weight"], router_bias=p["router.bias"])
+        del p
     torch.cuda.synchronize()
-    compute_ms_layer = a.elapsed_time(b) / (args.steps * len(resident))
-    del resident
+    ok = bool(torch.equal(out, ref))
+    del ref
     torch.cuda.empty_cache()
-    # host->device copy rate of pinned memory on this box (the bound)
+
+    # host->device copy rate of pinned memory on this box (the bound), per rank
     src = torch.empty(1 << 30, dtype=torch.uint8).pin_memory()
     dst = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
+    barrier(world)
+    h2d_gbs = -max_over_ranks(-_copy_gbs(src, dst), world)   # the slowest rank's link
+    del src, dst
+
+    # e2e: this rank's tokens in from pinned host memory, the stack's output back out
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty_like(x_host).pin_memory()
+    x_dev = torch.empty_like(x)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        out_host.copy_(stack(x_dev), non_blocking=True)
+    e2e = time_steps(e2e_step, args.steps, None, world)
+
+    load = {"rows": sum(st_rows) // max(args.steps, 1), "experts_staged": sum(st_experts) // max(args.steps, 1),
+            "staged_bytes": int(h2d_per_step), "parity": ok}
+    loads = [None] * world
+    if world > 1:
+        dist.all_gather_object(loads, load)
+    else:
+        loads = [load]
+    all_ok = all(l["parity"] for l in loads)
+
+    ref_engine = None
+    if world == 1 and not args.no_extra:
+        ref_engine = _reference_engine_ms(args, shape, states, x, layers, dev)
+
+    line = None
+    if rank == 0:
+        achieved = max(l["staged_bytes"] for l in loads) / (ms * 1e-3) / 1e9
+        full_bytes = layers * El * stack.layers[0].bytes_per_expert
+        line = {"metric": METRIC, "value": T * layers / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+                "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic (seeded weights, Zipf router bias)",
+                "config": {"workload": args.workload, "tokens": T, "layers": layers, "zipf_s": zipf_s,
+                           "parallelism": f"ep{world}" if world > 1 else "single GPU",
+                           "streaming": "blockstreamer_b200.streaming (expert-granular: hit experts only, "
+                                        f"{groups} id ranges whose GEMMs start as each lands, 2 device slots)",
+                           "value_is": "tokens x layers / step time",
+                           "l2": "inputs larger than L2 (up to 1.69 GB of weights staged per layer)"},
+                "parity": "ok" if all_ok else "MISMATCH vs resident layers",
+                "per_rank_load": [{"rank": r, **l} for r, l in enumerate(loads)],
+                "roofline": {"bound": "host link", "achieved": achieved, "peak": h2d_gbs, "unit": "GB/s",
+                             "frac": achieved / h2d_gbs, "traffic": max(l["staged_bytes"] for l in loads),
+                             "kernel": "host->device weight staging per step (busiest rank, all layers)",
+                             "peak_source": "measured pinned 1 GiB host->device copy on this box (slowest rank)",
+                             "all_experts_bytes_per_step": full_bytes},
+                "e2e": {"value": T * layers / (e2e * 1e-3), "unit": "tokens/s",
+                        "h2d_bytes_per_step": x.numel() * 2 * world, "d2h_bytes_per_step": x.numel() * 2 * world,
+                        "api": "blockstreamer_b200.streaming.%s" % type(stack).__name__},
+                "clocks": clk.summary(),
+                "gpu_launches": (sum(LAUNCHES.values()) - 2 + 2 * groups + (2 if world > 1 else 0))
+                * layers * args.steps}
+        if ref_engine is not None:
+            line["reference_engine"] = ref_engine
+    if exchange is not None:
+        exchange.close()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if not all_ok:
+        raise SystemExit(3)
+
+
+def _copy_gbs(src, dst):
+    st = torch.cuda.current_stream()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     dst.copy_(src, non_blocking=True)
     a.record(st)
     for _ in range(3):
         dst.copy_(src, non_blocking=True)
     b.record(st)
     torch.cuda.synchronize()
-    h2d_gbs = 3 * (1 << 30) / (a.elapsed_time(b) * 1e-3) / 1e9
-    del src, dst
-    # e2e: tokens in from pinned host memory, the stack's output back out
-    x_host = x.cpu().pin_memory()
-    out_host = torch.empty_like(x_host).pin_memory()
-    x_dev = torch.empty_like(x)
-    a.record(st)
-    for _ in range(args.steps):
-        x_dev.copy_(x_host, non_blocking=True)
-        o, _ = model(x_dev)
-        out_host.copy_(o, non_blocking=True)
-    b.record(st)
+    return 3 * src.numel() / (a.elapsed_time(b) * 1e-3) / 1e9
+
+
+def _reference_engine_ms(args, shape, states, x, layers, dev):
+    """The same layers as B200GptOssMLP blocks driven by the reference's own
+    StreamedModel (whole-block staging, prefetch_ahead=1), for comparison."""
+    import types
+    ref_dir = os.path.join(REPO, "baseline", "_ref")
+    if not os.path.exists(os.path.join(ref_dir, "streamer.py")):
+        return {"unavailable": "the reference package is not installed under baseline/_ref"}
+    sys.path.insert(0, ref_dir)
+    from streamer import StreamedModel  # the reference's own streaming engine
+    from blockstreamer_b200 import B200GptOssMLP
+    cfg = types.SimpleNamespace(hidden_size=shape.hidden, intermediate_size=shape.intermediate,
+                                num_local_experts=shape.experts, num_experts_per_tok=shape.top_k,
+                                swiglu_limit=7.0)
+    blocks = []
+    for s in states:
+        mlp = B200GptOssMLP(cfg)
+        mlp.load_state_dict(s, strict=True, assign=True)
+        blocks.append(mlp)
+    model = StreamedModel(blocks, device=dev, prefetch_ahead=1, dtype=None)
+    xs = x.view(1, *x.shape)
+    for _ in range(args.warmup):
+        model(xs)
     torch.cuda.synchronize()
-    e2e_ms = a.elapsed_time(b) / args.steps
-    achieved = h2d_per_step / (ms * 1e-3) / 1e9
-    line = {"metric": METRIC, "value": T * layers / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 1,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (seeded weights, Zipf router bias)",
-            "config": {"workload": args.workload, "tokens": T, "layers": layers, "zipf_s": zipf_s,
-                       "streaming": "reference StreamedModel (baseline/_ref/streamer.py), prefetch_ahead=1, "
-                                    "pinned host weights, functional_call binding",
-                       "value_is": "tokens x layers / step time",
-                       "expert_rows_layer0_max_min": [int(hist.max()), int(hist.min())],
-                       "experts_hit_layer0": int((hist > 0).sum()),
-                       "l2": "inputs larger than L2 (1.69 GB of weights streamed per layer)"},
-            "roofline": {"bound": "host link", "achieved": achieved, "peak": h2d_gbs, "unit": "GB/s",
-                         "frac": achieved / h2d_gbs, "traffic": h2d_per_step,
-                         "kernel": "host->device weight streaming per step (all layers)",
-                         "peak_source": "measured pinned 1 GiB host->device copy on this box"},
-            "layer_roofline": {"compute_ms_per_layer_resident": compute_ms_layer,
-                               "h2d_ms_per_layer_at_peak": h2d_per_step / layers / (h2d_gbs * 1e9) * 1e3,
-                               "stream_ms_per_layer": ms / layers},
-            "e2e": {"value": T * layers / (e2e_ms * 1e-3), "unit": "tokens/s",
-                    "h2d_bytes_per_step": x.numel() * 2, "d2h_bytes_per_step": x.numel() * 2,
-                    "api": "reference StreamedModel over blockstreamer_b200.B200GptOssMLP"},
-            "clocks": clk.summary(), "gpu_launches": 10 * layers * args.steps}
-    print(json.dumps(line), flush=True)
+    b0 = model.stats()["transfer_bytes"]
+    ms = time_steps(lambda: model(xs), args.steps, None, 1)
+    h2d = (model.stats()["transfer_bytes"] - b0) / args.steps
     model.close()
+    return {"engine": "reference StreamedModel (baseline/_ref/streamer.py), prefetch_ahead=1, whole-block staging",
+            "ms_per_step": ms, "value": x.shape[0] * layers / (ms * 1e-3), "unit": "tokens/s",
+            "h2d_bytes_per_step": h2d}
+
+
+def run_trace(args):
+    """One step of the workload under torch.profiler (CPU + CUDA activity), the
+    role of the reference's trace export (benchmark.py:153-174): the chrome
+    trace goes to DIR/trace.json, and a summary (kernels by total time, copies,
+    and how long copies and kernels ran at the same time) is printed."""
+    from blockstreamer_b200.streaming import EXPERT_TENSORS, StreamedMoEStack
+    from blockstreamer_b200.synthetic import zipf_router_bias
+    key, case_id, T = parse_workload(args.workload)
+    shape = CASES[key]
+    dev = torch.device("cuda", 0)
+    os.makedirs(args.trace, exist_ok=True)
+    if case_id == 5:      # the streamed stack (2 layers keep the trace small)
+        states = []
+        for li in range(2):
+            p = make_layer(shape, 10 * case_id + li, device=dev)
+            p["router.bias"] = zipf_router_bias(shape, 1.2, 10 * case_id + li).to(dev)
+            states.append({n: t.cpu().pin_memory() for n, t in p.items()})
+            del p
+        stack = StreamedMoEStack(states, shape.top_k, dev)
+        x = make_tokens(T, shape.hidden, case_id, device=dev)
+        step = lambda: stack(x)
+        what = "blockstreamer_b200.streaming.StreamedMoEStack, 2 layers"
+    else:
+        p = make_layer(shape, case_id, device=dev)
+        x = make_tokens(T, shape.hidden, case_id, device=dev)
+        w = [p["experts." + n] for n in EXPERT_TENSORS]
+        step = lambda: kernels.moe_forward(x, *w, shape.top_k, router_weight=p["router.weight"],
+                                           router_bias=p["router.bias"])
+        what = "kernels.moe_forward -> bs_moe_forward, one layer, eager"
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    acts = [torch.profiler.ProfilerActivity.CPU, torch.profiler.ProfilerActivity.CUDA]
+    with torch.profiler.profile(activities=acts) as prof:
+        step()
+        torch.cuda.synchronize()
+    path = os.path.join(args.trace, "trace.json")
+    prof.export_chrome_trace(path)
+    with open(path) as f:
+        events = json.load(f)["traceEvents"]
+    kern = [e for e in events if e.get("cat") == "kernel"]
+    copies = [e for e in events if e.get("cat") in ("gpu_memcpy", "gpu_memset")]
+    by_name = {}
+    for e in kern:
+        n = e["name"].replace("(anonymous namespace)::", "").split("(")[0]
+        c, d = by_name.get(n, (0, 0.0))
+        by_name[n] = (c + 1, d + float(e["dur"]))
+
+    def spans(evs):
+        return sorted((float(e["ts"]), float(e["ts"]) + float(e["dur"])) for e in evs)
+
+    def union(iv):
+        out = []
+        for a, b in iv:
+            if out and a <= out[-1][1]:
+                out[-1][1] = max(out[-1][1], b)
+            else:
+                out.append([a, b])
+        return out
+
+    ku, cu = union(spans(kern)), union(spans(copies))
+    both = 0.0
+    i = j = 0
+    while i < len(ku) and j < len(cu):
+        lo, hi = max(ku[i][0], cu[j][0]), min(ku[i][1], cu[j][1])
+        both += max(0.0, hi - lo)
+        if ku[i][1] < cu[j][1]:
+            i += 1
+        else:
+            j += 1
+    allv = spans(kern + copies)
+    summary = {"workload": args.workload, "what": what, "trace": path,
+               "gpu_activity": bool(kern), "span_us": (allv[-1][1] - allv[0][0]) if allv else 0.0,
+               "kernel_busy_us": sum(b - a for a, b in ku), "copy_busy_us": sum(b - a for a, b in cu),
+               "copy_and_kernel_overlap_us": both, "copies": len(copies),
+               "kernels": [{"name": n, "launches": c, "total_us": round(d, 1)}
+                           for n, (c, d) in sorted(by_name.items(), key=lambda kv: -kv[1][1])]}
+    print(json.dumps(summary), flush=True)
 
 
 def main():
@@ -1010,9 +1159,14 @@ def main():
     ap.add_argument("--no-graph", action="store_true", help="launch every step eagerly")
     ap.add_argument("--ep-transport", choices=["p2p", "nccl"], default="p2p",
                     help="N > 1: exchange rows over peer memory (library kernels) or NCCL all-to-all")
+    ap.add_argument("--trace", metavar="DIR", default=None,
+                    help="instead of timing: profile one step of the workload with torch.profiler, write "
+                         "DIR/trace.json and print a summary of its GPU activity (1 GPU)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.trace:
+        return run_trace(args)
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))
         world = int(os.environ.get("WORLD_SIZE", "1"))
