@@ -331,7 +331,7 @@ def run_reference(args, rank, world):
 STAGES = ("router", "dispatch", "gate_up", "down", "combine")
 LAUNCHES = {"router": 3, "dispatch": 4, "gate_up": 1, "down": 1, "combine": 1}  # router: 2 at T <= 64
 ALGOS = {"auto": kernels.ALGO_AUTO, "gemv": kernels.ALGO_GEMV, "tcgen05": kernels.ALGO_TCGEN05,
-         "mx": kernels.ALGO_MX, "fused": kernels.ALGO_FUSED}
+         "mx": kernels.ALGO_MX, "fused": kernels.ALGO_FUSED, "tcgen05_pair": kernels.ALGO_TCGEN05_PAIR}
 
 
 def layer_stages(x, p, k, algo, bufs):

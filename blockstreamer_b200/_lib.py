@@ -23,7 +23,7 @@ BS_ERR_TIMEOUT = 5
 BS_ERR_UNSUPPORTED = 6
 
 BS_BF16, BS_F32, BS_I32, BS_I64 = 0, 1, 2, 3
-ALGO_AUTO, ALGO_GEMV, ALGO_TCGEN05, ALGO_MX, ALGO_FUSED = 0, 1, 2, 3, 4
+ALGO_AUTO, ALGO_GEMV, ALGO_TCGEN05, ALGO_MX, ALGO_FUSED, ALGO_TCGEN05_PAIR = 0, 1, 2, 3, 4, 5
 
 _c = ctypes
 _vp, _i64, _i32, _f32, _sz = _c.c_void_p, _c.c_int64, _c.c_int, _c.c_float, _c.c_size_t

@@ -40,6 +40,10 @@ int tc_grouped_launch(int mode, const void* x, const int32_t* offsets, int64_t r
                       const void* blocks, const void* scales, const void* bias, int bias_f32,
                       float alpha, float limit, void* out, cudaStream_t st);
 bool tc_supported(const void* scales, int64_t K, int64_t N);
+int tc_pair_launch(int mode, const void* x, const int32_t* offsets, int64_t rows_total,
+                   int64_t max_rows_per_expert, int64_t E, int64_t K, int64_t N, const void* blocks,
+                   const void* scales, const void* bias, int bias_f32, float alpha, float limit, void* out,
+                   cudaStream_t st);
 // Decode path (decode.cu): router + dispatch + block-scaled expert MMAs + combine, T <= 64.
 bool decode_supported(int64_t T, int64_t H, int64_t I, int64_t E, int64_t k);
 size_t decode_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_t k);
@@ -80,7 +84,8 @@ int check_expert_args(const char* fn, const void* x, const void* blocks, const v
   BS_ARG(E <= 1024, "%s: at most 1024 experts", fn);
   BS_ARG(rows_total < (int64_t)INT32_MAX && N < (int64_t)INT32_MAX, "%s: sizes too large", fn);
   BS_ARG(bias_dtype == BS_BF16 || bias_dtype == BS_F32, "%s: bias dtype must be bf16 or f32", fn);
-  BS_ARG(algo >= BS_ALGO_AUTO && algo <= BS_ALGO_TCGEN05, "%s: unknown algo %d", fn, algo);
+  BS_ARG((algo >= BS_ALGO_AUTO && algo <= BS_ALGO_TCGEN05) || algo == BS_ALGO_TCGEN05_PAIR,
+         "%s: unknown algo %d", fn, algo);
   BS_ALIGNED16(x, "x");
   BS_ALIGNED16(blocks, "blocks");
   return BS_OK;
@@ -102,8 +107,8 @@ int gate_up(const void* x, const int32_t* offsets, int64_t rows_total, int64_t m
   if (a == BS_ALGO_GEMV)
     return gemv_gate_up_launch(x, offsets, rows_total, E, H, I, blocks, scales, bias, bf32, alpha,
                                limit, h, st);
-  return tc_grouped_launch(0, x, offsets, rows_total, max_rows, E, H, 2 * I, blocks, scales, bias,
-                           bf32, alpha, limit, h, st);
+  auto launch = a == BS_ALGO_TCGEN05_PAIR ? tc_pair_launch : tc_grouped_launch;
+  return launch(0, x, offsets, rows_total, max_rows, E, H, 2 * I, blocks, scales, bias, bf32, alpha, limit, h, st);
 }
 
 int down(const void* h, const int32_t* offsets, int64_t rows_total, int64_t max_rows, int64_t E,
@@ -118,8 +123,8 @@ int down(const void* h, const int32_t* offsets, int64_t rows_total, int64_t max_
   const int bf32 = bias_dtype == BS_F32;
   if (a == BS_ALGO_GEMV)
     return gemv_plain_launch(h, offsets, rows_total, E, I, H, blocks, scales, bias, bf32, y, st);
-  return tc_grouped_launch(1, h, offsets, rows_total, max_rows, E, I, H, blocks, scales, bias,
-                           bf32, 0.f, 0.f, y, st);
+  auto launch = a == BS_ALGO_TCGEN05_PAIR ? tc_pair_launch : tc_grouped_launch;
+  return launch(1, h, offsets, rows_total, max_rows, E, I, H, blocks, scales, bias, bf32, 0.f, 0.f, y, st);
 }
 
 struct Workspace {
@@ -191,7 +196,8 @@ extern "C" int bs_mxfp4_matmul(const void* x, int64_t m, int64_t K, const void* 
   const int a = pick_algo(algo, m, 1, scales, K, N);
   if (a == BS_ALGO_GEMV)
     return gemv_plain_launch(x, nullptr, m, 1, K, N, blocks, scales, bias, 0, out, st);
-  return tc_grouped_launch(1, x, nullptr, m, m, 1, K, N, blocks, scales, bias, 0, 0.f, 0.f, out, st);
+  auto launch = a == BS_ALGO_TCGEN05_PAIR ? tc_pair_launch : tc_grouped_launch;
+  return launch(1, x, nullptr, m, m, 1, K, N, blocks, scales, bias, 0, 0.f, 0.f, out, st);
 }
 
 namespace bs {
@@ -224,7 +230,7 @@ int moe_forward_impl(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, 
   BS_ARG(T >= 0 && H > 0 && I > 0 && E > 0 && k > 0 && k <= E, "bs_moe_forward: bad sizes");
   BS_ARG((router_weight == nullptr) == (router_bias == nullptr),
          "bs_moe_forward: router weight and bias go together");
-  BS_ARG(algo >= BS_ALGO_AUTO && algo <= BS_ALGO_FUSED, "bs_moe_forward: unknown algo %d", algo);
+  BS_ARG(algo >= BS_ALGO_AUTO && algo <= BS_ALGO_TCGEN05_PAIR, "bs_moe_forward: unknown algo %d", algo);
   if (T == 0) return BS_OK;
   BS_ARG(workspace, "bs_moe_forward: null workspace");
   BS_ALIGNED16(workspace, "workspace");

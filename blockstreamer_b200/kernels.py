@@ -15,7 +15,7 @@ from dataclasses import dataclass
 import torch
 
 from . import _lib
-from ._lib import ALGO_AUTO, ALGO_FUSED, ALGO_GEMV, ALGO_MX, ALGO_TCGEN05  # noqa: F401  (re-exported)
+from ._lib import ALGO_AUTO, ALGO_FUSED, ALGO_GEMV, ALGO_MX, ALGO_TCGEN05, ALGO_TCGEN05_PAIR  # noqa: F401  (re-exported)
 
 _DT = {torch.bfloat16: _lib.BS_BF16, torch.float32: _lib.BS_F32,
        torch.int32: _lib.BS_I32, torch.int64: _lib.BS_I64}

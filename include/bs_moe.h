@@ -51,8 +51,12 @@ enum bs_algo {
   BS_ALGO_TCGEN05 = 2,  /* tcgen05/TMEM grouped GEMM (prefill shapes)                 */
   BS_ALGO_MX = 3,       /* bs_moe_forward only, T <= 64: tcgen05 block-scaled MMAs on  */
                         /* the e2m1 codes (activations as four e2m1 terms)            */
-  BS_ALGO_FUSED = 4     /* bs_moe_forward only, T <= 8, on request: the whole layer in */
+  BS_ALGO_FUSED = 4,    /* bs_moe_forward only, T <= 8, on request: the whole layer in */
                         /* ONE cooperative persistent kernel                           */
+  BS_ALGO_TCGEN05_PAIR = 5  /* on request: the grouped GEMM run by CTA pairs          */
+                            /* (tcgen05.mma.cta_group::2, M = 256 weight rows); same   */
+                            /* results as BS_ALGO_TCGEN05, measured slower at gpt-oss  */
+                            /* shapes                                                  */
 };
 
 /* Library identity. */

@@ -7,8 +7,11 @@ same library kernels, so routing and results must agree), once through the
 peer-memory exchange and once through NCCL all-to-all, over three successive
 calls (the peer-memory flags and buffers are reused across calls) and, for
 the peer-memory path, two replays of a captured CUDA graph; the two exchanges
-must give bit-identical outputs.  Last, rank 0 calls the exchange while rank 1
-does not: rank 0's bounded waits must run out and report BS_ERR_TIMEOUT.
+must give bit-identical outputs.  Then the expert-granular streamed stack
+over the same exchange (each rank pinning only its slice of two layers) must
+equal the resident layers chained on the rank's tokens.  Last, rank 0 calls
+the exchange while rank 1 does not: rank 0's bounded waits must run out and
+report BS_ERR_TIMEOUT.
 Exits non-zero on any mismatch."""
 
 import datetime
@@ -23,7 +26,8 @@ sys.path.insert(0, REPO)
 
 from blockstreamer_b200 import _lib, kernels  # noqa: E402
 from blockstreamer_b200.expert_parallel import CudaOps, ExpertParallelMoE, P2PExchange, shard_experts  # noqa: E402
-from blockstreamer_b200.synthetic import CASES, LayerShape, make_layer, make_tokens  # noqa: E402
+from blockstreamer_b200.streaming import EXPERT_TENSORS, StreamedEPStack  # noqa: E402
+from blockstreamer_b200.synthetic import CASES, LayerShape, make_layer, make_tokens, zipf_router_bias  # noqa: E402
 
 
 def rel_l2(a, b):
@@ -88,6 +92,36 @@ def main():
         same_bits = torch.equal(outs["p2p"], outs["nccl"])
         print(f"rank {rank} {name}: p2p and nccl outputs bit-identical: {same_bits}", flush=True)
         ok &= same_bits
+    # The streamed stack over expert parallelism: each rank pins only its
+    # slice of two Zipf-routed layers and stages the hit experts of it; its
+    # output must equal the resident layers chained on the same tokens.
+    shape = cases[0][1]
+    T = 64 * world
+    Tr = T // world
+    states = []
+    for li in range(2):
+        st = make_layer(shape, 30 + li, device=dev)
+        st["router.bias"] = zipf_router_bias(shape, 1.6, 30 + li).to(dev) * 4.0
+        states.append(st)
+    x_all = make_tokens(T, shape.hidden, 31, device=dev)
+    x = x_all[rank * Tr:(rank + 1) * Tr].contiguous()
+    ex = P2PExchange(None, shape.experts, shape.hidden, Tr, shape.top_k, dev)
+    lo, hi = rank * (shape.experts // world), (rank + 1) * (shape.experts // world)
+    host = [{n: (t[lo:hi] if n.startswith("experts.") else t).cpu() for n, t in st.items()} for st in states]
+    stack = StreamedEPStack(host, shape.top_k, ex, groups=2)
+    for call in range(2):
+        out = stack(x)
+        torch.cuda.synchronize()
+    ref = x
+    for st in states:
+        ref, _, _ = kernels.moe_forward(ref, *[st["experts." + n] for n in EXPERT_TENSORS], shape.top_k,
+                                        router_weight=st["router.weight"], router_bias=st["router.bias"])
+    same = torch.equal(out, ref)
+    print(f"rank {rank} streamed EP stack: staged experts per layer {stack.stats.experts_staged[-2:]} "
+          f"of {hi - lo}, equal to resident layers: {same}", flush=True)
+    ok &= same
+    ex.close()
+
     # A peer that never takes part: rank 0 sends, rank 1 does not.  Rank 0's
     # waits for rank 1's counts and rows run out (bounded, ~2 s each) and
     # report BS_ERR_TIMEOUT through the status word; the context stays usable.
