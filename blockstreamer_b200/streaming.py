@@ -191,7 +191,11 @@ class StreamedEPStack:
     [r E/R, (r+1) E/R) of every layer pinned, routes its own tokens, exchanges
     rows over peer memory (``expert_parallel.P2PExchange``), stages the
     experts of its slice that received rows from any rank, computes them and
-    returns the rows.  Collective: every rank calls ``forward`` in step."""
+    returns the rows.  Collective: every rank calls ``forward`` in step.
+
+    ``states``: per layer, the router tensors and either the layer's full
+    expert tensors ([E, ...], sliced here) or only this rank's slice
+    ([E/R, ...], as a rank that pins nothing else holds them)."""
 
     def __init__(self, states: list[dict], top_k: int, exchange, groups: int = 4, hit_only: bool = True,
                  alpha: float = kernels.ALPHA, limit: float = kernels.LIMIT, algo: int = kernels.ALGO_AUTO):
@@ -199,8 +203,16 @@ class StreamedEPStack:
         self.device = exchange.device
         R, me, E = exchange.R, exchange.me, exchange.E
         self.El = E // R
-        sl = (me * self.El, (me + 1) * self.El)
-        self.layers = [HostLayer(s, self.device, expert_slice=sl) for s in states]
+        self.layers = []
+        for st in states:
+            rows = st["experts." + EXPERT_TENSORS[0]].shape[0]
+            if rows == E:
+                sl = (me * self.El, (me + 1) * self.El)
+            elif rows == self.El:
+                sl = None
+            else:
+                raise ValueError(f"StreamedEPStack: {rows} experts per layer is neither {E} nor this rank's {self.El}")
+            self.layers.append(HostLayer(st, self.device, expert_slice=sl))
         self.k, self.groups, self.hit_only = top_k, groups, hit_only
         self.alpha, self.limit, self.algo = alpha, limit, algo
         self.E = E
