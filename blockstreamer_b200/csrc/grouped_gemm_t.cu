@@ -289,7 +289,12 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_t_kernel(
         ptx::tc_fence_after();
         for (int ks = 0; ks < KS; ++ks, ++gi) {
           const int sb = gi % kStagesB, sa = gi % kStagesA;
-          if (!ptx::mbar_wait(adone(sa), (gi / kStagesA) & 1, abort_flag)) { ok = false; break; }
+          // the weight slot (dequant) and the token tile (TMA) of this step
+          if (!ptx::mbar_wait(adone(sa), (gi / kStagesA) & 1, abort_flag) ||
+              !ptx::mbar_wait(fullB(sb), (gi / kStagesB) & 1, abort_flag)) {
+            ok = false;
+            break;
+          }
           ptx::tc_fence_after();
           const uint64_t bd = bdesc0 + (uint64_t)((sb * kBBytes) >> 4);
           const uint32_t at = a_t0 + sa * (kBK / 2);
@@ -386,14 +391,25 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_t_kernel(
           const uint32_t s0 = A[kACodes + (2 * half) * 64 + jrow];
           const uint32_t s1 = A[kACodes + (2 * half + 1) * 64 + jrow];
           const E2M1Pool p0 = make_e2m1_pool(s0), p1 = make_e2m1_pool(s1);
-          e2m1x8_decode(b0.x, s0, p0, v + 0);
-          e2m1x8_decode(b0.y, s0, p0, v + 4);
-          e2m1x8_decode(b0.z, s0, p0, v + 8);
-          e2m1x8_decode(b0.w, s0, p0, v + 12);
-          e2m1x8_decode(b1.x, s1, p1, v + 16);
-          e2m1x8_decode(b1.y, s1, p1, v + 20);
-          e2m1x8_decode(b1.z, s1, p1, v + 24);
-          e2m1x8_decode(b1.w, s1, p1, v + 28);
+          if (s0 - 2u <= 250u && s1 - 2u <= 250u) {   // byte-table form for both scales: branch-free
+            e2m1x8_to_bf16x8(b0.x, p0, v + 0);
+            e2m1x8_to_bf16x8(b0.y, p0, v + 4);
+            e2m1x8_to_bf16x8(b0.z, p0, v + 8);
+            e2m1x8_to_bf16x8(b0.w, p0, v + 12);
+            e2m1x8_to_bf16x8(b1.x, p1, v + 16);
+            e2m1x8_to_bf16x8(b1.y, p1, v + 20);
+            e2m1x8_to_bf16x8(b1.z, p1, v + 24);
+            e2m1x8_to_bf16x8(b1.w, p1, v + 28);
+          } else {
+            e2m1x8_decode(b0.x, s0, p0, v + 0);
+            e2m1x8_decode(b0.y, s0, p0, v + 4);
+            e2m1x8_decode(b0.z, s0, p0, v + 8);
+            e2m1x8_decode(b0.w, s0, p0, v + 12);
+            e2m1x8_decode(b1.x, s1, p1, v + 16);
+            e2m1x8_decode(b1.y, s1, p1, v + 20);
+            e2m1x8_decode(b1.z, s1, p1, v + 24);
+            e2m1x8_decode(b1.w, s1, p1, v + 28);
+          }
         }
         // rows (2p, 2p + 1) of one feature into one word; staging[p][feature]
         const int odd = jrow & 1, pr = jrow >> 1;
@@ -410,8 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_t_kernel(
         ptx::tmem_wait_st();
         ptx::tc_fence_before();
         // the staging tile may be overwritten once the whole group passed here
-        ok = named_and(bar_id, 128, warp_wait(fullB(gi % kStagesB), (gi / kStagesB) & 1, abort_flag));
-        if (!ok) break;
+        named_sync(bar_id, 128);
         if (lane == 0) ptx::mbar_arrive(adone(s));
       }
     }

@@ -108,14 +108,17 @@ def main():
     ex = P2PExchange(None, shape.experts, shape.hidden, Tr, shape.top_k, dev)
     lo, hi = rank * (shape.experts // world), (rank + 1) * (shape.experts // world)
     host = [{n: (t[lo:hi] if n.startswith("experts.") else t).cpu() for n, t in st.items()} for st in states]
-    stack = StreamedEPStack(host, shape.top_k, ex, groups=2)
+    # tensor-core kernels on both sides (at 64 tokens AUTO would take the
+    # decode path for the resident layers, a different algorithm)
+    stack = StreamedEPStack(host, shape.top_k, ex, groups=2, algo=kernels.ALGO_TCGEN05)
     for call in range(2):
         out = stack(x)
         torch.cuda.synchronize()
     ref = x
     for st in states:
         ref, _, _ = kernels.moe_forward(ref, *[st["experts." + n] for n in EXPERT_TENSORS], shape.top_k,
-                                        router_weight=st["router.weight"], router_bias=st["router.bias"])
+                                        router_weight=st["router.weight"], router_bias=st["router.bias"],
+                                        algo=kernels.ALGO_TCGEN05)
     same = torch.equal(out, ref)
     print(f"rank {rank} streamed EP stack: staged experts per layer {stack.stats.experts_staged[-2:]} "
           f"of {hi - lo}, equal to resident layers: {same}", flush=True)
