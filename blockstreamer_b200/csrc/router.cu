@@ -26,6 +26,21 @@ template <> __device__ __forceinline__ float ld_f32<__nv_bfloat16>(const __nv_bf
   return __bfloat162float(*p);
 }
 
+// Eight consecutive elements (16-byte aligned) as floats.
+__device__ __forceinline__ void ld8_f32(const float* p, float (&o)[8]) {
+  const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+  o[0] = a.x; o[1] = a.y; o[2] = a.z; o[3] = a.w; o[4] = b.x; o[5] = b.y; o[6] = b.z; o[7] = b.w;
+}
+__device__ __forceinline__ void ld8_f32(const __nv_bfloat16* p, float (&o)[8]) {
+  const uint4 q = *reinterpret_cast<const uint4*>(p);
+  const uint32_t u[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    o[2 * i] = __uint_as_float(u[i] << 16);
+    o[2 * i + 1] = __uint_as_float(u[i] & 0xFFFF0000u);
+  }
+}
+
 __device__ __forceinline__ float round_logit(float v, bool bf16_logits) {
   return bf16_logits ? __bfloat162float(__float2bfloat16_rn(v)) : v;
 }
@@ -140,7 +155,47 @@ __global__ void __launch_bounds__(256) router_fused_kernel(
   }
 }
 
-// Small T: warp per expert; lane strides over H in 4-element steps.
+// Small T: warp per expert, MaxT tokens per CTA; each lane takes 8
+// consecutive elements of H per step as 16-byte loads (H a multiple of 8,
+// 16-byte aligned x and W), so every load feeds 8 FMAs per token.
+template <typename XT, typename WT, int MaxT>
+__global__ void __launch_bounds__(256) router_logits_small_vec_kernel(
+    const XT* __restrict__ x, const WT* __restrict__ W, const WT* __restrict__ b, int T, int H,
+    int E, bool bf16_logits, float* __restrict__ logits) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x & 31;
+  if (warp >= E) return;
+  const int t0 = blockIdx.y * MaxT;
+  x += (int64_t)t0 * H;
+  logits += (int64_t)t0 * E;
+  T = min(T - t0, MaxT);
+  const WT* w = W + (int64_t)warp * H;
+  float acc[MaxT];
+#pragma unroll
+  for (int t = 0; t < MaxT; ++t) acc[t] = 0.f;
+  for (int h = lane * 8; h < H; h += 256) {
+    float wv[8];
+    ld8_f32(w + h, wv);
+#pragma unroll
+    for (int t = 0; t < MaxT; ++t) {
+      if (t < T) {
+        float xv[8];
+        ld8_f32(x + (int64_t)t * H + h, xv);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc[t] = fmaf(xv[i], wv[i], acc[t]);
+      }
+    }
+  }
+#pragma unroll
+  for (int t = 0; t < MaxT; ++t) {
+    float v = acc[t];
+#pragma unroll
+    for (int off = 16; off; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    if (lane == 0 && t < T) logits[(int64_t)t * E + warp] = round_logit(v + ld_f32(b + warp), bf16_logits);
+  }
+}
+
+// Small T, any H or alignment: warp per expert; lane strides over H.
 template <typename XT, typename WT, int MaxT>
 __global__ void __launch_bounds__(256) router_logits_small_kernel(
     const XT* __restrict__ x, const WT* __restrict__ W, const WT* __restrict__ b, int T, int H,
@@ -215,7 +270,10 @@ int launch_router(const void* x, const void* w, const void* b, int T, int H, int
     // one warp per (expert, 8 tokens): E/8 x T/8 CTAs, so that even a few
     // tokens spread over the SMs
     const dim3 grid((unsigned)cdiv(E, 8), (unsigned)cdiv(T, 8));
-    router_logits_small_kernel<XT, WT, 8><<<grid, 256, 0, st>>>(xp, wp, bp, T, H, E, bf16_logits, logits);
+    if (H % 8 == 0 && (((uintptr_t)x | (uintptr_t)w) & 15) == 0)
+      router_logits_small_vec_kernel<XT, WT, 8><<<grid, 256, 0, st>>>(xp, wp, bp, T, H, E, bf16_logits, logits);
+    else
+      router_logits_small_kernel<XT, WT, 8><<<grid, 256, 0, st>>>(xp, wp, bp, T, H, E, bf16_logits, logits);
     BS_LAUNCHED();
     router_topk_kernel<<<(unsigned)cdiv(T, 8), 256, 0, st>>>(logits, T, E, k, scores, i32, i64);
     BS_LAUNCHED();
