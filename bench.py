@@ -42,6 +42,7 @@ from blockstreamer_b200.synthetic import (CASES, algorithmic_bytes, algorithmic_
 
 METRIC = "MoE-layer tokens/s at gpt-oss-120b shape"
 DEFAULT_WORKLOAD = "gptoss120b-prefill-8192"
+BACKWARD_WORKLOAD = "gptoss120b-prefill-8192-backward"
 EXTRA_WORKLOADS = ("gptoss20b-prefill-4096", "gptoss120b-decode-1", "gptoss120b-decode-8",
                    "gptoss120b-decode-64")
 PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
@@ -59,6 +60,8 @@ SUSTAINED_REGION_S = 1.0
 
 
 def parse_workload(name: str):
+    if name == BACKWARD_WORKLOAD:
+        return "gptoss120b", 6, 8192
     if name.startswith("gptoss120b-zipf-"):   # gptoss120b-zipf-<T>-streamed
         return "gptoss120b", 5, int(name.split("-")[2])
     if name.startswith("gptoss120b-prefill-"):
@@ -717,6 +720,18 @@ def run_ours(args, rank, world, local):
     shape = CASES[key]
     if case_id == 5:
         return run_bench_streamed(args, rank, world, shape, case_id, T_total)
+    if case_id == 6:   # the expert backward alone (also part of the default run's configs)
+        if world > 1:
+            raise SystemExit("the backward workload runs on one GPU")
+        r = measure_backward(args, local)
+        line = {"metric": "expert-layer backward tokens/s at gpt-oss-120b shape", "value": r["value"],
+                "unit": r["unit"], "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": r["ms_per_step"], "higher_is_better": True, "scaling": "strong",
+                "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": {"workload": args.workload, "tokens": T_total, "what": r["what"]},
+                "roofline": r["roofline"]}
+        print(json.dumps(line), flush=True)
+        return
     if world > 1:
         return run_bench_ep(args, rank, world, local, shape, case_id, T_total)
     line = measure(args.workload, args, world, local)
@@ -730,7 +745,7 @@ def run_ours(args, rank, world, local):
             extra[w] = {n: r[n] for n in ("value", "unit", "ms_per_step", "roofline", "layer_roofline", "e2e",
                                           "clocks", "gpu_launches")}
             extra[w]["config"] = r["config"]
-        extra["gptoss120b-prefill-8192-backward"] = measure_backward(args, local)
+        extra[BACKWARD_WORKLOAD] = measure_backward(args, local)
         torch.cuda.empty_cache()
         line["configs"] = extra
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

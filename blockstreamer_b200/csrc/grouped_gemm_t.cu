@@ -339,6 +339,17 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_t_kernel(
       const bool fv = feat < Kw;
       const uint32_t taddr = tbase + ((uint32_t)(q * 32) << 16);
       for (int c0 = 0; c0 < t.nmma; c0 += 16) {
+        // EPI 1: the chunk's 16 pre-activation pairs are requested before the
+        // accumulator load, so their HBM latency is paid once per chunk
+        float2 gp[16];
+        if (EPI == 1) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int n = c0 + i;
+            gp[i] = (n < t.nrows && fv) ? *reinterpret_cast<const float2*>(g + (t.r0 + n) * 2 * Kw + 2 * feat)
+                                        : make_float2(0.f, 0.f);
+          }
+        }
         uint32_t v[16];
         ptx::tmem_ld_32x32b_x16(taddr + c0, v);
         ptx::tmem_wait_ld();
@@ -351,9 +362,8 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_t_kernel(
           if (EPI == 0) {
             out[row * Kw + feat] = __bfloat16_as_ushort(__float2bfloat16_rn(acc));
           } else {
-            const float2 gp = *reinterpret_cast<const float2*>(g + row * 2 * Kw + 2 * feat);
             float dgate, dup;
-            swiglu_backward(gp.x, gp.y, acc, alpha, limit, dgate, dup);
+            swiglu_backward(gp[i].x, gp[i].y, acc, alpha, limit, dgate, dup);
             *reinterpret_cast<uint32_t*>(out + row * 2 * Kw + 2 * feat) = pack_bf16x2(dgate, dup);
           }
         }
