@@ -43,13 +43,19 @@ namespace {
 
 // h[r, i] = (clamp(up) + 1) * min(gate, L) * sigmoid(alpha * min(gate, L)),
 // gate = g[r, 2i], up = g[r, 2i + 1] (gptoss.py:130-135), from fp32 g.
-__global__ void __launch_bounds__(256) swiglu_rows_kernel(const float2* __restrict__ g, int64_t n_pairs,
-                                                          float alpha, float limit, uint16_t* __restrict__ h) {
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n_pairs; i += (int64_t)gridDim.x * blockDim.x) {
-    const float2 v = g[i];
-    const float gate = fminf(v.x, limit);
-    const float up = fminf(fmaxf(v.y, -limit), limit);
-    h[i] = __bfloat16_as_ushort(__float2bfloat16_rn((up + 1.0f) * (gate / (1.0f + expf(-alpha * gate)))));
+__device__ __forceinline__ float swiglu_exact(float gate, float up, float alpha, float limit) {
+  gate = fminf(gate, limit);
+  up = fminf(fmaxf(up, -limit), limit);
+  return (up + 1.0f) * (gate / (1.0f + expf(-alpha * gate)));
+}
+
+// Two outputs per thread (16-byte loads of g, 4-byte stores of h); n_pairs even.
+__global__ void __launch_bounds__(256) swiglu_rows_kernel(const float4* __restrict__ g, int64_t n_pairs,
+                                                          float alpha, float limit, uint32_t* __restrict__ h) {
+  const int64_t n2 = n_pairs / 2;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n2; i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 v = g[i];
+    h[i] = pack_bf16x2(swiglu_exact(v.x, v.y, alpha, limit), swiglu_exact(v.z, v.w, alpha, limit));
   }
 }
 
@@ -250,8 +256,8 @@ extern "C" int bs_moe_backward(const void* x, int64_t T, int64_t H, int64_t I, i
                          w.dispatch_bytes, st));
   BS_TRY(tc_grouped_launch(2, w.xp, w.offsets, S, S, E, H, 2 * I, gate_up_blocks, gate_up_scales, gate_up_bias, bf32,
                            0.f, 0.f, w.g, st));
-  swiglu_rows_kernel<<<grid_for(S * I), 256, 0, st>>>(reinterpret_cast<const float2*>(w.g), S * I, alpha, limit,
-                                                      w.h);
+  swiglu_rows_kernel<<<grid_for(S * I / 2), 256, 0, st>>>(reinterpret_cast<const float4*>(w.g), S * I, alpha,
+                                                          limit, reinterpret_cast<uint32_t*>(w.h));
   BS_LAUNCHED();
   BS_TRY(tc_grouped_launch(1, w.h, w.offsets, S, S, E, I, H, down_blocks, down_scales, down_bias, bf32, 0.f, 0.f,
                            w.y, st));
