@@ -333,6 +333,16 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_t_kernel(
     uint32_t j = 0;
     for (int item = blockIdx.x; item < total; item += gridDim.x, ++j) {
       const Tile t = decode_item(off, ipre, E, MT, item);
+      if (EPI == 1 && t.mt * kBM + q * 32 < Kw) {
+        // while the tile's MMAs run: pull this warp's 32 features (256 bytes)
+        // of every row's pre-activation into L2 for the drain below
+        const float* gq = g + 2 * (t.mt * kBM + q * 32);
+        for (int n = lane; n < t.nrows; n += 32) {
+          const float* pr = gq + (t.r0 + n) * 2 * Kw;
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(pr));
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(pr + 32));
+        }
+      }
       if (!warp_wait(accfull, j & 1, abort_flag)) break;
       ptx::tc_fence_after();
       const int feat = t.mt * kBM + q * 32 + lane;
