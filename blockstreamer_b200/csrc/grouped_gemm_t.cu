@@ -152,7 +152,9 @@ __device__ __forceinline__ void swiglu_backward(float gate, float up, float dh, 
                                                 float& dgate, float& dup) {
   const float gc = fminf(gate, limit);
   const float uc = fminf(fmaxf(up, -limit), limit);
-  const float sg = 1.0f / (1.0f + expf(-alpha * gc));
+  // the hardware exponential and division, as the forward epilogue: their
+  // few-ulp error is far below the bf16 rounding of dg
+  const float sg = __fdividef(1.0f, 1.0f + __expf(-alpha * gc));
   const float glu = gc * sg;
   dup = (up >= -limit && up <= limit) ? dh * glu : 0.f;
   dgate = (gate <= limit) ? dh * (uc + 1.0f) * (sg + gc * alpha * sg * (1.0f - sg)) : 0.f;
