@@ -29,19 +29,23 @@
 //  4. decode_combine_kernel out[t] = bf16(sum over the k slots), fp32 sum.
 //
 // Work item of 2/3: 128 weight rows of one expert and a group of up to 16 of
-// its tokens.  One CTA per SM: warp 4 issues the TMA copies (weight tiles
-// [128 rows x 256 codes] as stored, the B term rows, per-item scale blocks),
-// warp 5 the MMAs, warps 6-9 (one per 32-lane TMEM subpartition) write every
-// stage's scale factors into TMEM with tcgen05.st, warps 0-3 drain the
-// accumulators.  On this GPU each tcgen05.mma, tcgen05.cp and tcgen05.commit
-// takes ~100 cycles of the tensor pipe, so the scale factors stay out of it:
-// the pipe runs 4 MMAs + 1 commit per 16 KB stage, less than the stage's HBM
-// time.
+// its tokens, K in stages of 256.  The items' stages are cut into equal
+// contiguous ranges, one per CTA (stream-K): at one token the gate_up
+// projection is 180 items of 12 stages on 148 SMs, which whole items would
+// leave 32 SMs doing two.  An item split across CTAs is finished by the CTA
+// holding its last stage, which adds the others' partial sums (written to
+// the workspace, counted by a flag per CTA) before its epilogue.
 //
-// Measured here: code that runs once per item (epilogue, routing) executes
-// with a cold instruction cache while the weights saturate HBM, where each
-// fetch of a few instructions waits on the memory system; such code is kept
-// short and in loops rather than unrolled where its latency is exposed.
+// One CTA per SM: warp 4 issues the TMA copies (weight tiles [128 rows x 256
+// codes] as stored, the B term rows, per-item scale blocks), warp 5 the MMAs,
+// warps 6-13 (two groups of four, one warp per 32-lane TMEM subpartition,
+// alternating stages) write every stage's scale factors into TMEM with
+// tcgen05.st, warps 0-3 drain the accumulators.  Measured on this GPU: one
+// thread issues a block-scaled MMA every ~115 cycles and a commit in ~90, so
+// the MMA thread's own instructions set the stage rate -- its loop has no
+// divisions and advances descriptors by addition -- and one group of
+// scale-factor warps (loads, TMEM stores and their wait: ~0.6 us a stage)
+// would be slower than the MMAs.
 #include "bs_common.cuh"
 #include "bs_ptx.cuh"
 #include "bs_topk.cuh"
@@ -56,7 +60,7 @@ constexpr int kTerms = 4;       // e2m1 terms per activation
 constexpr int kRTok = 16;       // tokens per router CTA
 constexpr int kKC = 256;        // K elements per pipeline stage: 128 bytes of codes per row, 4 MMAs
 constexpr int kBM = 128;        // weight rows per item (MMA M)
-constexpr int kThreads = 320;   // warps 0-3 epilogue, 4 TMA, 5 MMA, 6-9 scale factors
+constexpr int kThreads = 448;   // warps 0-3 epilogue, 4 TMA, 5 MMA, 6-9 and 10-13 scale factors
 constexpr int kTmemCols = 512;
 constexpr int kSfStageCols = 24;  // per stage: SFA 2 groups x 4 columns, SFB 2 groups x 4 or 8 columns
 constexpr int kMaxStages = 12;
@@ -64,6 +68,9 @@ constexpr int kMaxRing = 4;       // per-item buffers
 constexpr int kGroupTok = 16;     // tokens per group: an item's B is 4 x 16 = 64 rows at most
 constexpr int kMaxGroups = 1024 + 2048 / kGroupTok;
 constexpr int kRankMax = 8192;    // token x expert logits ranked in shared memory (32 KB)
+constexpr int kMaxCtas = 256;     // grid of the expert launches (one CTA per SM, at most this)
+constexpr long long kFlagWait = 2000000000LL;  // ~1 s of SM clock: bound of a wait on another CTA
+constexpr int64_t kPrefetchMax = 48ll << 20;  // the next projection's weights pulled into L2 at most
 
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
@@ -80,6 +87,22 @@ __device__ __forceinline__ bool named_and(int id, int n, bool v) {
       : "r"((uint32_t)v), "r"(id), "r"(n)
       : "memory");
   return r != 0;
+}
+
+// Bounded wait until *f >= target (acquire, GPU scope); raises *abort and
+// returns false after ~kFlagWait cycles or when another thread raised it.
+__device__ __forceinline__ bool wait_flag(const unsigned* f, unsigned target, volatile int* abort) {
+  if (ptx::ld_acquire_gpu(f) >= target) return true;
+  const long long t0 = clock64();
+  while (ptx::ld_acquire_gpu(f) < target) {
+    if (*abort) return false;
+    if (clock64() - t0 > kFlagWait) {
+      *abort = 1;
+      return false;
+    }
+    __nanosleep(64);
+  }
+  return true;
 }
 
 struct DecodeMeta {  // lives in the workspace
@@ -130,11 +153,14 @@ template <typename WT>
 __global__ void __launch_bounds__(256) decode_route_kernel(
     const __nv_bfloat16* __restrict__ x, const WT* __restrict__ W, const WT* __restrict__ b,
     int T, int H, int E, int bf16_logits, float* __restrict__ logits, uint8_t* __restrict__ xq,
-    uint8_t* __restrict__ xs, int gp) {
+    uint8_t* __restrict__ xs, int gp, unsigned* __restrict__ flags, int nflags) {
   __shared__ float red[8][kRTok];
   pdl_wait();  // x comes from the previous kernel in the stream
   pdl_launch();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // the expert launches' partial-sum flags start at zero every layer
+  if (blockIdx.x == 0 && blockIdx.y == 0)
+    for (int i = tid; i < nflags; i += blockDim.x) flags[i] = 0u;
 
   // x -> four e2m1 terms; 16 lanes per 32-value block, two values a lane
   {
@@ -248,6 +274,16 @@ struct MxArgs {
   uint8_t* hs;            //             rows (4 r + term) of gp_out bytes
   int gp_out;
   float* y;               // MODE 1 out: [rows][Nw] fp32
+  // items split across CTAs: the partial sums of every piece but the last,
+  // [CTA][token of the group][row], and per CTA a count of the epilogue warps
+  // that wrote theirs (zeroed by the route kernel)
+  float* part;
+  unsigned* flags;
+  // MODE 0: the down projection's weights, pulled into L2 once the routing
+  // is known (NULL: not pulled); bytes of codes and of scales per expert
+  const uint8_t* pf_codes;
+  const uint8_t* pf_scales;
+  int64_t pf_cb, pf_sb;
   int* status;
 };
 constexpr int kBStage = 0;     // one B tile per pipeline stage
@@ -395,6 +431,60 @@ __device__ void route_dispatch(const MxArgs& p, int* scratch, int* s_slot, int2*
   __syncthreads();
 }
 
+// MODE 0 epilogue of four tokens (chunk c) once their accumulators are read:
+// clamped SwiGLU of the (gate, up) row pairs, and h re-split into four e2m1
+// terms with their e8m0 scales for the down projection.  Rows alternate
+// gate / up: h_i (i = row / 2) sits in lanes 2m, 2m+1; a 32-block of h is 64
+// rows = warps (0,1) or (2,3); the byte of codes (h_i, h_i+1), i even, is
+// written by lane 4m'.  `dry`: the same instructions with every store
+// skipped, run once by the epilogue warps while the first stages stream, so
+// that the real pass does not fetch its instructions while HBM is saturated
+// (a few microseconds otherwise).  Out of line: one copy serves both.
+__device__ __noinline__ void h_terms(const MxArgs& p, float a0, float a1, float a2, float a3, int c, int ntok,
+                                     bool rv, int row_lo, int i, int warp, int lane, float (*red)[4][4],
+                                     bool unrolled, bool dry) {
+  const float acc[4] = {a0, a1, a2, a3};
+  float r[4];
+#pragma unroll
+  for (int jj = 0; jj < 4; ++jj) {
+    const float other = __shfl_xor_sync(0xffffffffu, acc[jj], 1);
+    const float gate = (lane & 1) ? other : acc[jj], up = (lane & 1) ? acc[jj] : other;
+    r[jj] = swiglu(gate, up, p.alpha, p.limit);
+  }
+  const int I = p.Nw >> 1;
+  auto term_step = [&](int term) {
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+      const float m = group_max<32>(fabsf(r[jj]));
+      if (lane == 0) red[term & 1][warp][jj] = m;
+    }
+    named_sync(1, 128);
+#pragma unroll
+    for (int jj = 0; jj < 4; ++jj) {
+      const int tok = c * 4 + jj;
+      const uint32_t sb = e8m0_for_max(fmaxf(red[term & 1][warp][jj], red[term & 1][warp ^ 1][jj]));
+      const float q = r[jj] * exp2_neg(sb);
+      const float qn = __shfl_down_sync(0xffffffffu, q, 2);  // h_{i+1}
+      const uint32_t byte = ptx::e2m1x2_from_f32(q, qn);
+      r[jj] -= ptx::e2m1_lo_to_f32(byte) * exp2_pos(sb);
+      if (tok < ntok && rv && !dry) {
+        const int64_t hr = (int64_t)(row_lo + tok) * kTerms + term;
+        if ((lane & 3) == 0) p.hq[hr * (I / 2) + (i >> 1)] = (uint8_t)byte;
+        if (lane == 0 && !(warp & 1)) p.hs[hr * p.gp_out + (i >> 5)] = (uint8_t)sb;
+      }
+    }
+  };
+  // a single chunk (few tokens: its latency is exposed) loops over the
+  // terms; more chunks (throughput) run them unrolled
+  if (!unrolled) {
+#pragma unroll 1
+    for (int term = 0; term < kTerms; ++term) term_step(term);
+  } else {
+#pragma unroll
+    for (int term = 0; term < kTerms; ++term) term_step(term);
+  }
+}
+
 // MODE 0: B = the four term rows of tokens (every token's when resident or
 // per stage; the MMA computes them all and the epilogue keeps the expert's);
 // MODE 1: B = the group's own rows of h.
@@ -486,10 +576,64 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
 
   const int per_e = (Nw + kBM - 1) / kBM;
   const int n_items = s_ngrp * per_e;
-  const int n_my = n_items > (int)blockIdx.x ? (n_items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  // Stream-K: the items' K stages, item after item, cut into gridDim.x equal
+  // ranges of consecutive stages.  CTA c takes range c and works through its
+  // pieces (the parts of items inside the range) from the top down, so that
+  // the head pieces of an item split across CTAs finish first, on lower CTAs,
+  // and its tail piece -- the owner, which adds their partial sums before the
+  // epilogue -- runs last, on the highest of them.  Every CTA holds at most
+  // one head piece: its first.
+  // 32-bit arithmetic (stages x grid < 2^31, checked by decode_supported):
+  // a 64-bit division costs about a microsecond of one thread's time here
+  const int G_ = (int)gridDim.x;
+  const int n_st = n_items * nkc;
+  auto range_lo = [&](int c) { return n_st * c / G_; };
+  auto nonempty = [&](int c) { return n_st >= G_ || range_lo(c) < range_lo(c + 1); };
+  const int lo = range_lo(blockIdx.x), hi = range_lo(blockIdx.x + 1);
+  const int top = hi > lo ? (hi - 1) / nkc : 0;
+  const int n_pc = hi > lo ? top - lo / nkc + 1 : 0;
+  struct Piece {
+    int item, kc0, kc1;
+  };
+  auto piece = [&](int pc) {
+    Piece q;
+    q.item = top - pc;
+    const int s0 = q.item * nkc;
+    q.kc0 = lo > s0 ? lo - s0 : 0;
+    q.kc1 = hi - s0 < nkc ? hi - s0 : nkc;
+    return q;
+  };
   const uint32_t smem0 = ptx::smem_addr(smem);
   const uint32_t sf_base = (uint32_t)(p.nacc * nb);  // TMEM column of stage 0's scale factors
-  auto item_of = [&](int it) { return (int)blockIdx.x + it * (int)gridDim.x; };
+
+  // MODE 0: the down projection's weights of the routed experts into L2 once
+  // this CTA's own copies are issued (HBM would otherwise idle from the end
+  // of this launch's stream to the first copies of the next); CTA c pulls
+  // slice c of their concatenation.  One warp.
+  auto prefetch_next = [&]() {
+    if (MODE != 0 || !p.pf_codes || s_ngrp > 32) return;
+    const uint32_t full = 0xffffffffu;
+    const int ex = lane < s_ngrp ? (s_grp[lane].x & 0xFFFF) : -1;
+    const int prev = __shfl_up_sync(full, ex, 1);
+    const uint32_t firsts = __ballot_sync(full, lane < s_ngrp && (lane == 0 || prev != ex));
+    const int D = __popc(firsts);
+    if ((int64_t)D * (p.pf_cb + p.pf_sb) <= kPrefetchMax) {
+      for (int part = 0; part < 2; ++part) {
+        const int64_t per = part == 0 ? p.pf_cb : p.pf_sb;
+        const uint8_t* base = part == 0 ? p.pf_codes : p.pf_scales;
+        const int64_t a = ((int64_t)D * per * blockIdx.x / G_) & ~(int64_t)15;
+        const int64_t b = ((int64_t)D * per * (blockIdx.x + 1) / G_) & ~(int64_t)15;
+        for (int d = 0; d < D; ++d) {
+          const int e = __shfl_sync(full, ex, __fns(firsts, 0, d + 1));
+          const int64_t u0 = a > d * per ? a : d * per, u1 = b < (d + 1) * per ? b : (d + 1) * per;
+          constexpr int64_t kChunk = 16384;
+          for (int64_t o = u0 + lane * kChunk; o < u1; o += 32 * kChunk)
+            ptx::bulk_prefetch_l2(base + (int64_t)e * per + (o - d * per),
+                                  (uint32_t)(u1 - o < kChunk ? u1 - o : kChunk));
+        }
+      }
+    }
+  };
   // B rows of an item: MODE 0 every token's (or, gathered, the group's
   // tokens'), MODE 1 the group's
   const bool gather = p.b_mode == kBGather;
@@ -503,8 +647,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
     // limit at 64 tokens).
     const uint32_t full = 0xffffffffu;
     int g = 0, n_issued = 0;
+    int s = 0, ph = 0;  // slot and parity of stage g: g % S, (g / S) & 1 (no divisions in the loop)
     bool ok = true;
-    if (lane == 0 && p.b_mode == kBResident && n_my > 0) {
+    if (lane == 0 && p.b_mode == kBResident && n_pc > 0) {
       // every token's B tiles and scale rows, once
       const uint32_t rb = ptx::smem_addr(res);
       ptx::mbar_arrive_expect_tx(resb, (uint32_t)(nkc * nb * 128 + kTerms * p.T * p.gp));
@@ -512,14 +657,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
       if (nfull < nkc) ptx::tma_load_2d(rb + nfull * nb * 128, &pa.tm_b, resb, nfull * 128, 0);
       ptx::bulk_load(rb + L.res_b, p.bsf, (uint32_t)(kTerms * p.T * p.gp), resb);
     }
-    for (int it = 0; it < n_my && ok; ++it) {
-      const int item = item_of(it);
+    for (int pc = 0; pc < n_pc && ok; ++pc) {
+      const Piece q = piece(pc);
+      const int item = q.item;
       const int2 gr = s_grp[item / per_e];
       const int e = gr.x & 0xFFFF, r0 = (item % per_e) * kBM, ntok = gr.x >> 16;
       const int nrows = min(kBM, Nw - r0), nbv = nbrows(gr), b0 = brow0(gr);
-      const int b = it % NR;
+      const int b = pc % NR;
       bool w = true;
-      if (lane == 0 && it >= NR) w = ptx::mbar_wait(bfree(b), ((it / NR) - 1) & 1, &abort_flag);
+      if (lane == 0 && pc >= NR) w = ptx::mbar_wait(bfree(b), ((pc / NR) - 1) & 1, &abort_flag);
       if (!__shfl_sync(full, w, 0)) break;
       const uint32_t sbt = ptx::smem_addr(ring0 + b * L.ring), sca = sbt + L.ring_b, scb = sca + L.ring_sa;
       // gathered B: this lane's token (its first term row)
@@ -544,9 +690,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
         ptx::bulk_load(scb + lane * kTerms * p.gp, p.bsf + (int64_t)trow * p.gp, (uint32_t)(kTerms * p.gp),
                        itemb(b));
       ++n_issued;
-      for (int kc = 0; kc < nkc; ++kc, ++g) {
-        const int s = g % S;
-        if (lane == 0 && g >= S) w = ptx::mbar_wait(empty(s), ((g / S) - 1) & 1, &abort_flag);
+      for (int kc = q.kc0; kc < q.kc1; ++kc, ++g) {
+        if (lane == 0 && g >= S) w = ptx::mbar_wait(empty(s), ph ^ 1, &abort_flag);
         if (!__shfl_sync(full, w, 0)) {
           ok = false;
           break;
@@ -561,6 +706,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
         // one 4-row box per token of the group (the stage's count covers exactly these)
         if (gather && lane < ntok)
           ptx::tma_load_2d(sa + kBM * 128 + lane * kTerms * 128, &pa.tm_b, data(s), kc * 128, trow);
+        if (++s == S) s = 0, ph ^= 1;
       }
     }
     if (lane == 0 && abort_flag) {
@@ -571,46 +717,53 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
         ptx::mbar_wait(data(gg % S), (gg / S) & 1, &quiet, 100000000LL);
       for (int i2 = max(0, n_issued - NR); i2 < n_issued; ++i2)
         ptx::mbar_wait(itemb(i2 % NR), (i2 / NR) & 1, &quiet, 100000000LL);
-      if (p.b_mode == kBResident && n_my > 0) ptx::mbar_wait(resb, 0, &quiet, 100000000LL);
+      if (p.b_mode == kBResident && n_pc > 0) ptx::mbar_wait(resb, 0, &quiet, 100000000LL);
     }
     __syncwarp();
+    if (!abort_flag) prefetch_next();
   } else if (warp == 5) {
     // ---------------------------------------------------------- MMA issue (one thread)
     if (lane == 0) {
-      int g = 0;
+      // one thread whose per-stage instructions are the issue rate: no
+      // divisions in the loop, descriptors advanced by addition
+      int g = 0, s = 0, ph = 0;
       bool ok = true;
-      if (p.b_mode == kBResident && n_my > 0) ok = ptx::mbar_wait(resb, 0, &abort_flag);
-      for (int it = 0; it < n_my && ok; ++it) {
-        const int item = item_of(it);
-        const int2 gr = s_grp[item / per_e];
+      if (p.b_mode == kBResident && n_pc > 0) ok = ptx::mbar_wait(resb, 0, &abort_flag);
+      for (int pc = 0; pc < n_pc && ok; ++pc) {
+        const Piece q = piece(pc);
+        const int2 gr = s_grp[q.item / per_e];
         const int N = ((nbrows(gr) + 15) / 16) * 16;
-        const int ab = it % p.nacc, b = it % NR;
-        if (it >= p.nacc && !ptx::mbar_wait(accempty(ab), ((it / p.nacc) - 1) & 1, &abort_flag)) break;
-        if (p.b_mode == kBItem && !ptx::mbar_wait(itemb(b), (it / NR) & 1, &abort_flag)) break;
+        const int ab = pc % p.nacc, b = pc % NR;
+        if (pc >= p.nacc && !ptx::mbar_wait(accempty(ab), ((pc / p.nacc) - 1) & 1, &abort_flag)) break;
+        if (p.b_mode == kBItem && !ptx::mbar_wait(itemb(b), (pc / NR) & 1, &abort_flag)) break;
         ptx::tc_fence_after();
         const uint32_t acc = tmem + ab * nb;
         const uint32_t bt = p.b_mode == kBItem ? ptx::smem_addr(ring0 + b * L.ring) : ptx::smem_addr(res);
-        for (int kc = 0; kc < nkc; ++kc, ++g) {
-          const int s = g % S;
-          if (!ptx::mbar_wait(data(s), (g / S) & 1, &abort_flag) ||
-              !ptx::mbar_wait(sffull(s), (g / S) & 1, &abort_flag)) {
+        const uint32_t id0 = ptx::idesc_mxf4(N, 0, 0), id2 = ptx::idesc_mxf4(N, 2, 2);
+        const bool b_in_stage = p.b_mode == kBStage || gather;
+        // smem descriptors' address field is (address >> 4): advancing a
+        // descriptor by a 16-byte multiple adds to it
+        const uint64_t ad0 = ptx::sdesc_kmajor_sw128(smem0);
+        const uint64_t bd_item = ptx::sdesc_kmajor_sw128(bt) + (uint64_t)((q.kc0 * nb * 128) >> 4);
+        for (int kc = q.kc0; kc < q.kc1; ++kc, ++g) {
+          if (!ptx::mbar_wait(data(s), ph, &abort_flag) || !ptx::mbar_wait(sffull(s), ph, &abort_flag)) {
             ok = false;
             break;
           }
           ptx::tc_fence_after();
-          const uint32_t sa = smem0 + s * L.stage;
-          const uint64_t ad = ptx::sdesc_kmajor_sw128(sa);
-          const uint64_t bd = ptx::sdesc_kmajor_sw128((p.b_mode == kBStage || gather) ? sa + kBM * 128
-                                                                                      : bt + kc * nb * 128);
+          const uint64_t ad = ad0 + (uint64_t)((s * L.stage) >> 4);
+          const uint64_t bd = b_in_stage ? ad + (kBM * 128 >> 4) : bd_item + (uint64_t)(((kc - q.kc0) * nb * 128) >> 4);
           // scale factors (written by warps 6-9): SFA at columns 4q, SFB at
           // 8 + 4 nbk q for groups q = 0, 1 of four k-blocks
           const uint32_t sf = tmem + sf_base + s * kSfStageCols;
-          for (int i = 0; i < 4 && kc * kKC + i * 64 < K; ++i) {
-            const uint32_t id = 2 * (i & 1);
-            ptx::mma_mxf4_ss(acc, ad + 2 * i, bd + 2 * i, ptx::idesc_mxf4(N, id, id), sf + 4 * (i >> 1),
-                             sf + 8 + 4 * nbk * (i >> 1), (kc | i) != 0);
-          }
+          const int nm = (K - kc * kKC) >= kKC ? 4 : (K - kc * kKC) / 64;
+          const bool acc0 = kc != q.kc0;
+          ptx::mma_mxf4_ss(acc, ad, bd, id0, sf, sf + 8, acc0);
+          if (nm > 1) ptx::mma_mxf4_ss(acc, ad + 2, bd + 2, id2, sf, sf + 8, 1);
+          if (nm > 2) ptx::mma_mxf4_ss(acc, ad + 4, bd + 4, id0, sf + 4, sf + 8 + 4 * nbk, 1);
+          if (nm > 3) ptx::mma_mxf4_ss(acc, ad + 6, bd + 6, id2, sf + 4, sf + 8 + 4 * nbk, 1);
           ptx::tc_commit(empty(s));
+          if (++s == S) s = 0, ph ^= 1;
         }
         if (ok) {
           ptx::tc_commit(accfull(ab));
@@ -624,29 +777,35 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
     // This warp writes its own 32-lane subpartition; the four hold copies.
     // SFA word (q, j) of lane l: scales of row l + 32 j, k-blocks 4q..4q+3;
     // SFB word (q, j): B row l + 32 j.
+    // Two groups of four (warps 6-9: even stages, 10-13: odd stages): one
+    // stage's loads, TMEM stores and their wait take longer than its MMAs.
     const uint32_t lanes = (uint32_t)(32 * (warp & 3)) << 16;
-    int g = 0;
+    const int grp = warp >= 10;
+    int g = 0, s = 0, ph = 0;  // stage g's slot and parity
     bool ok = true;
-    if (p.b_mode == kBResident && n_my > 0) {
+    if (p.b_mode == kBResident && n_pc > 0) {
       bool w = true;
       if (lane == 0) w = ptx::mbar_wait(resb, 0, &abort_flag);
       ok = __shfl_sync(0xffffffffu, w, 0);
     }
-    for (int it = 0; it < n_my && ok; ++it) {
-      const int item = item_of(it);
-      const int2 gr = s_grp[item / per_e];
-      const int r0 = (item % per_e) * kBM;
+    for (int pc = 0; pc < n_pc && ok; ++pc) {
+      const Piece q = piece(pc);
+      const int2 gr = s_grp[q.item / per_e];
+      const int r0 = (q.item % per_e) * kBM;
       const int nrows = min(kBM, Nw - r0), nbv = nbrows(gr);
-      const int b = it % NR;
+      const int b = pc % NR;
       bool w = true;
-      if (lane == 0) w = ptx::mbar_wait(itemb(b), (it / NR) & 1, &abort_flag);
+      if (lane == 0) w = ptx::mbar_wait(itemb(b), (pc / NR) & 1, &abort_flag);
       if (!__shfl_sync(0xffffffffu, w, 0)) break;
       const uint8_t* sca = ring0 + b * L.ring + L.ring_b;
       const uint8_t* scb = p.b_mode == kBResident ? res + L.res_b : sca + L.ring_sa;
-      for (int kc = 0; kc < nkc; ++kc, ++g) {
-        const int s = g % S;
+      for (int kc = q.kc0; kc < q.kc1; ++kc, ++g) {
+        if ((g & 1) != grp) {
+          if (++s == S) s = 0, ph ^= 1;
+          continue;
+        }
         if (g >= S) {
-          if (lane == 0) w = ptx::mbar_wait(empty(s), ((g / S) - 1) & 1, &abort_flag);
+          if (lane == 0) w = ptx::mbar_wait(empty(s), ph ^ 1, &abort_flag);
           if (!__shfl_sync(0xffffffffu, w, 0)) {
             ok = false;
             break;
@@ -686,23 +845,30 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
         ptx::tc_fence_before();
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(sffull(s));
+        if (++s == S) s = 0, ph ^= 1;
       }
     }
   } else {
     // ---------------------------------------------------------- epilogue
     const uint32_t lanes = (uint32_t)(32 * warp) << 16;
     bool ok = true;
-    for (int it = 0; it < n_my && ok; ++it) {
-      const int item = item_of(it);
+    if (MODE == 0 && n_pc > 0) h_terms(p, 0.f, 0.f, 0.f, 0.f, 0, 0, false, 0, 0, warp, lane, red, false, true);
+    for (int pc = 0; pc < n_pc && ok; ++pc) {
+      const Piece q = piece(pc);
+      const int item = q.item;
       const int2 gr = s_grp[item / per_e];
       const int e = gr.x & 0xFFFF, ntok = gr.x >> 16, row_lo = gr.y, r0 = (item % per_e) * kBM;
       const int nrows = min(kBM, Nw - r0);
-      const int ab = it % p.nacc;
+      const int ab = pc % p.nacc;
       const int lrow = 32 * warp + lane;
       const bool rv = lrow < nrows;
       const int64_t grow = (int64_t)e * Nw + r0 + lrow;
+      // a head piece of a split item leaves its sums to the item's tail piece
+      // (the owner), which adds those of CTAs [c_first, this one)
+      const bool owner = q.kc1 == nkc;
+      const int c_first = (owner && q.kc0 > 0) ? ((item * nkc + 1) * G_ - 1) / n_st : (int)blockIdx.x;
       float bv = 0.f;
-      if (rv && p.bias)
+      if (owner && rv && p.bias)
         bv = p.bias_f32 ? static_cast<const float*>(p.bias)[grow]
                         : __bfloat162float(static_cast<const __nv_bfloat16*>(p.bias)[grow]);
       // per token j of the group: its accumulator column (MODE 0: the token's
@@ -714,27 +880,42 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
         col = (MODE == 0 && !gather) ? kTerms * (sl / p.k) : kTerms * lane;
         if (MODE == 1) wt = p.scores[sl];
       }
-      bool got = ptx::mbar_wait(accfull(ab), (it / p.nacc) & 1, &abort_flag);
+      bool got = ptx::mbar_wait(accfull(ab), (pc / p.nacc) & 1, &abort_flag);
+      for (int c2 = c_first; got && c2 < (int)blockIdx.x; ++c2)
+        if (nonempty(c2)) got = wait_flag(p.flags + c2, 4u, &abort_flag);
       if (!named_and(1, 128, got)) break;
       ptx::tc_fence_after();
       const uint32_t tl = tmem + lanes + ab * nb;
       const int nchunk = (ntok + 3) / 4;
       for (int c = 0; c < nchunk; ++c) {
-        float acc[4];
+        // the head pieces' sums of these four tokens: all loads in flight at once
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int c2 = c_first; c2 < (int)blockIdx.x; ++c2)
+          if (nonempty(c2)) {
+            const float* pp = p.part + ((int64_t)c2 * kGroupTok + c * 4) * kBM + lrow;
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) acc[jj] += __ldcg(pp + jj * kBM);
+          }
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
           const int cj = __shfl_sync(0xffffffffu, col, (c * 4 + jj) & 31);
           uint32_t u[4];
           ptx::tmem_ld_32x32b_x4(tl + cj, u);  // tokens past ntok read column 0, unused
           ptx::tmem_wait_ld();
-          acc[jj] = __uint_as_float(u[0]) + __uint_as_float(u[1]) + __uint_as_float(u[2]) +
-                    __uint_as_float(u[3]) + bv;
+          acc[jj] += __uint_as_float(u[0]) + __uint_as_float(u[1]) + __uint_as_float(u[2]) +
+                     __uint_as_float(u[3]) + bv;
         }
         if (c == nchunk - 1) {
           // accumulator drained: the MMAs of a later item may use it
           ptx::tc_fence_before();
           __syncwarp();
           if (lane == 0) ptx::mbar_arrive(accempty(ab));
+        }
+        if (!owner) {
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj)
+            if (c * 4 + jj < ntok && rv) p.part[((int64_t)blockIdx.x * kGroupTok + c * 4 + jj) * kBM + lrow] = acc[jj];
+          continue;
         }
         if (MODE == 1) {
 #pragma unroll
@@ -744,49 +925,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
             if (tok < ntok && rv) p.y[(int64_t)(row_lo + tok) * Nw + r0 + lrow] = acc[jj] * w;
           }
         } else {
-          // rows alternate gate / up: h_i (i = row / 2) sits in lanes 2m, 2m+1;
-          // a 32-block of h is 64 rows = warps (0,1) or (2,3); the byte of
-          // codes (h_i, h_i+1), i even, is written by lane 4m'
-          float r[4];
-#pragma unroll
-          for (int jj = 0; jj < 4; ++jj) {
-            const float other = __shfl_xor_sync(0xffffffffu, acc[jj], 1);
-            const float gate = (lane & 1) ? other : acc[jj], up = (lane & 1) ? acc[jj] : other;
-            r[jj] = swiglu(gate, up, p.alpha, p.limit);
-          }
-          const int i = (r0 + lrow) >> 1, I = Nw >> 1;
-          // a single pass (few tokens: its latency is exposed) loops over the
-          // terms; items with more tokens (throughput) run them unrolled
-          auto term_step = [&](int term) {
-#pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-              const float m = group_max<32>(fabsf(r[jj]));
-              if (lane == 0) red[term & 1][warp][jj] = m;
-            }
-            named_sync(1, 128);
-#pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-              const int tok = c * 4 + jj;
-              const uint32_t sb = e8m0_for_max(fmaxf(red[term & 1][warp][jj], red[term & 1][warp ^ 1][jj]));
-              const float q = r[jj] * exp2_neg(sb);
-              const float qn = __shfl_down_sync(0xffffffffu, q, 2);  // h_{i+1}
-              const uint32_t byte = ptx::e2m1x2_from_f32(q, qn);
-              r[jj] -= ptx::e2m1_lo_to_f32(byte) * exp2_pos(sb);
-              if (tok < ntok && rv) {
-                const int64_t hr = (int64_t)(row_lo + tok) * kTerms + term;
-                if ((lane & 3) == 0) p.hq[hr * (I / 2) + (i >> 1)] = (uint8_t)byte;
-                if (lane == 0 && !(warp & 1)) p.hs[hr * p.gp_out + (i >> 5)] = (uint8_t)sb;
-              }
-            }
-          };
-          if (nchunk == 1) {
-#pragma unroll 1
-            for (int term = 0; term < kTerms; ++term) term_step(term);
-          } else {
-#pragma unroll
-            for (int term = 0; term < kTerms; ++term) term_step(term);
-          }
+          h_terms(p, acc[0], acc[1], acc[2], acc[3], c, ntok, rv, row_lo, (r0 + lrow) >> 1, warp, lane, red,
+                  nchunk > 1, false);
         }
+      }
+      if (!owner) {
+        // this warp's partial sums are out: count it for the owner
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) atomicAdd(p.flags + blockIdx.x, 1u);
       }
     }
   }
@@ -897,7 +1044,8 @@ template <int MODE>
 int launch_mx(const MxArgs& a, cudaStream_t st) {
   const size_t smem = mx_smem(a.K, a.nb, a.b_mode, a.gp, a.stages, a.nsc).total;
   BS_CUDA(cudaFuncSetAttribute(decode_mx_kernel<MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  return launch_pdl(decode_mx_kernel<MODE>, dim3((unsigned)sm_count()), dim3(kThreads), smem, st, a);
+  return launch_pdl(decode_mx_kernel<MODE>, dim3((unsigned)std::min(sm_count(), kMaxCtas)), dim3(kThreads), smem, st,
+                    a);
 }
 
 }  // namespace
@@ -914,6 +1062,8 @@ struct DecodeWS {
   uint8_t* hq;
   uint8_t* hs;
   float* y;
+  float* part;
+  unsigned* flags;
   size_t total;
 };
 
@@ -937,6 +1087,8 @@ DecodeWS decode_carve(void* base, int64_t T, int64_t H, int64_t I, int64_t E, in
   w.hq = reinterpret_cast<uint8_t*>(take((size_t)S * kTerms * I / 2));
   w.hs = reinterpret_cast<uint8_t*>(take((size_t)S * kTerms * gp_of(I)));
   w.y = reinterpret_cast<float*>(take((size_t)S * H * 4));
+  w.part = reinterpret_cast<float*>(take((size_t)kMaxCtas * kGroupTok * kBM * 4));
+  w.flags = reinterpret_cast<unsigned*>(take((size_t)2 * kMaxCtas * 4));
   w.total = o;
   return w;
 }
@@ -946,8 +1098,11 @@ size_t decode_workspace_bytes(int64_t T, int64_t H, int64_t I, int64_t E, int64_
 }
 
 bool decode_supported(int64_t T, int64_t H, int64_t I, int64_t E, int64_t k) {
+  // the expert launches split (item, K stage) pairs over the grid in 32-bit arithmetic
+  const int64_t stages = kMaxGroups * std::max(cdiv(2 * I, (int64_t)kBM) * cdiv(H, (int64_t)kKC),
+                                               cdiv(H, (int64_t)kBM) * cdiv(I, (int64_t)kKC));
   return T >= 1 && T <= kMaxDecodeT && E <= 1024 && k <= 32 && H % 64 == 0 && I % 64 == 0 &&
-         (2 * I) % kBM == 0;
+         (2 * I) % kBM == 0 && stages * kMaxCtas < ((int64_t)1 << 31);
 }
 
 // The four-launch decode forward.  router_weight NULL: scores/indices are inputs.
@@ -969,12 +1124,12 @@ int decode_forward(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, in
     BS_TRY(launch_pdl(decode_route_kernel<float>, rgrid, dim3(256), 0, st,
                       static_cast<const __nv_bfloat16*>(x), static_cast<const float*>(rw),
                       static_cast<const float*>(rb), (int)T, (int)H, (int)E, 0, w.logits, w.xq, w.xs,
-                      gp_of(H)));
+                      gp_of(H), w.flags, 2 * kMaxCtas));
   } else {
     BS_TRY(launch_pdl(decode_route_kernel<__nv_bfloat16>, rgrid, dim3(256), 0, st,
                       static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(rw),
                       static_cast<const __nv_bfloat16*>(rb), (int)T, (int)H, (int)E, 1, w.logits, w.xq,
-                      w.xs, gp_of(H)));
+                      w.xs, gp_of(H), w.flags, 2 * kMaxCtas));
   }
   MxArgs a{};
   a.logits = rw ? w.logits : nullptr;
@@ -992,6 +1147,13 @@ int decode_forward(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, in
   a.limit = limit;
   a.bias_f32 = bias_f32;
   a.status = status;
+  a.part = w.part;
+  a.flags = w.flags;
+  // the routed experts' down weights are pulled into L2 during gate_up
+  a.pf_codes = static_cast<const uint8_t*>(dn_b);
+  a.pf_scales = static_cast<const uint8_t*>(dn_s);
+  a.pf_cb = H * (I / 2);
+  a.pf_sb = H * (I / 32);
   const CUtensorMapDataType u8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
   const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B;
   // gate_up: A = [E][2I][H/32][16], B = x terms of every token, out = h terms
@@ -1022,6 +1184,9 @@ int decode_forward(const void* x, int64_t T, int64_t H, int64_t I, int64_t E, in
   a.Nw = (int)H;
   a.K = (int)I;
   a.y = w.y;
+  a.flags = w.flags + kMaxCtas;
+  a.pf_codes = nullptr;
+  a.pf_scales = nullptr;
   BS_TRY(make_map_2d(&a.tm_a, u8, dn_b, (uint64_t)(I / 2), (uint64_t)(E * H), (uint64_t)(I / 2), 128, kBM, sw));
   a.nb = (int)((kTerms * std::min<int64_t>(T, kGroupTok) + 15) / 16 * 16);  // a group's tokens
   BS_TRY(plan_mx(a, {kBItem, kBStage}));
