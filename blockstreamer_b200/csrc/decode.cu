@@ -67,7 +67,6 @@ constexpr int kMaxStages = 12;
 constexpr int kMaxRing = 4;       // per-item buffers
 constexpr int kGroupTok = 16;     // tokens per group: an item's B is 4 x 16 = 64 rows at most
 constexpr int kMaxGroups = 1024 + 2048 / kGroupTok;
-constexpr int kRankMax = 8192;    // token x expert logits ranked in shared memory (32 KB)
 constexpr int kMaxCtas = 256;     // grid of the expert launches (one CTA per SM, at most this)
 constexpr long long kFlagWait = 2000000000LL;  // ~1 s of SM clock: bound of a wait on another CTA
 constexpr int64_t kPrefetchMax = 48ll << 20;  // the next projection's weights pulled into L2 at most
@@ -161,6 +160,10 @@ __global__ void __launch_bounds__(256) decode_route_kernel(
   // the expert launches' partial-sum flags start at zero every layer
   if (blockIdx.x == 0 && blockIdx.y == 0)
     for (int i = tid; i < nflags; i += blockDim.x) flags[i] = 0u;
+  // this CTA's router row on its way into L2 while the terms are computed
+  if (W && blockIdx.x < E && tid * 128 < H * (int)sizeof(WT))
+    for (int o = tid * 128; o < H * (int)sizeof(WT); o += 256 * 128)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(W + (int64_t)blockIdx.x * H) + o));
 
   // x -> four e2m1 terms; 16 lanes per 32-value block, two values a lane
   {
@@ -322,10 +325,11 @@ __device__ void route_dispatch(const MxArgs& p, int* scratch, int* s_slot, int2*
   const bool writer = blockIdx.x == 0;
   int* s_idx = scratch;
   int* cnt = scratch + n;
-  if (p.logits && T * E <= kRankMax) {
-    // rank every (token, expert): the number of experts ahead of it (higher
-    // logit, or equal and lower index; NaN counts as -inf); ranks < k are the
-    // top-k in order
+  if (p.logits && T * E <= kThreads) {
+    // rank every (token, expert), one per thread: the number of experts ahead
+    // of it (higher logit, or equal and lower index; NaN counts as -inf);
+    // ranks < k are the top-k in order.  Measured faster than the warp top-k
+    // below when every pair has its own thread, slower otherwise.
     float* lg = reinterpret_cast<float*>(scratch + n + E);
     float* sv = lg + T * E;  // [T][k] selected logits
     for (int i = tid; i < T * E; i += kThreads) {
@@ -338,6 +342,7 @@ __device__ void route_dispatch(const MxArgs& p, int* scratch, int* s_slot, int2*
       const float* row = lg + t * E;
       const float v = row[e];
       int r = 0;
+#pragma unroll 8
       for (int e2 = 0; e2 < E; ++e2) r += (row[e2] > v) | ((row[e2] == v) & (e2 < e));
       if (r < k) {
         s_idx[t * k + r] = e;
@@ -345,13 +350,15 @@ __device__ void route_dispatch(const MxArgs& p, int* scratch, int* s_slot, int2*
       }
     }
     __syncthreads();
-    if (writer)
-      for (int t = tid; t < T; t += kThreads) {
-        float sum = 0.f;
-        for (int j = 0; j < k; ++j) sum += expf(sv[t * k + j] - sv[t * k]);
-        for (int j = 0; j < k; ++j) p.scores[t * k + j] = expf(sv[t * k + j] - sv[t * k]) / sum;
+    if (writer)  // softmax over the k selected logits: a warp per token, a lane per slot (k <= 32)
+      for (int t = warp; t < T; t += kThreads / 32) {
+        const float ev = lane < k ? expf(sv[t * k + lane] - sv[t * k]) : 0.f;
+        float sum = ev;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if (lane < k) p.scores[t * k + lane] = ev / sum;
       }
-  } else if (p.logits) {
+  } else if (p.logits) {  // a warp per token
     for (int t = warp; t < T; t += kThreads / 32)
       warp_topk_any([&](int e2) { return __ldcg(p.logits + (int64_t)t * E + e2); }, E, k,
                     writer ? p.scores + (int64_t)t * k : nullptr, s_idx + t * k);
@@ -420,6 +427,7 @@ __device__ void route_dispatch(const MxArgs& p, int* scratch, int* s_slot, int2*
       continue;
     }
     int r = 0;
+#pragma unroll 8
     for (int j = 0; j < i; ++j) r += (s_idx[j] == e);
     const int pos = cnt[e] + r;
     s_slot[pos] = i;
@@ -449,7 +457,10 @@ __device__ __noinline__ void h_terms(const MxArgs& p, float a0, float a1, float 
   for (int jj = 0; jj < 4; ++jj) {
     const float other = __shfl_xor_sync(0xffffffffu, acc[jj], 1);
     const float gate = (lane & 1) ? other : acc[jj], up = (lane & 1) ? acc[jj] : other;
-    r[jj] = swiglu(gate, up, p.alpha, p.limit);
+    // the reference's clamped SwiGLU (gptoss.py:130-135) with the hardware
+    // exponential and division: a few ulp, far below the e2m1 terms' error
+    const float gc = fminf(gate, p.limit), uc = fminf(fmaxf(up, -p.limit), p.limit);
+    r[jj] = (uc + 1.0f) * __fdividef(gc, 1.0f + __expf(-p.alpha * gc));
   }
   const int I = p.Nw >> 1;
   auto term_step = [&](int term) {
@@ -458,7 +469,7 @@ __device__ __noinline__ void h_terms(const MxArgs& p, float a0, float a1, float 
       const float m = group_max<32>(fabsf(r[jj]));
       if (lane == 0) red[term & 1][warp][jj] = m;
     }
-    named_sync(1, 128);
+    named_sync(2 + (warp >> 1), 64);  // a 32-block of h: warps (0, 1) or (2, 3)
 #pragma unroll
     for (int jj = 0; jj < 4; ++jj) {
       const int tok = c * 4 + jj;
@@ -852,7 +863,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
     // ---------------------------------------------------------- epilogue
     const uint32_t lanes = (uint32_t)(32 * warp) << 16;
     bool ok = true;
-    if (MODE == 0 && n_pc > 0) h_terms(p, 0.f, 0.f, 0.f, 0.f, 0, 0, false, 0, 0, warp, lane, red, false, true);
     for (int pc = 0; pc < n_pc && ok; ++pc) {
       const Piece q = piece(pc);
       const int item = q.item;
@@ -879,6 +889,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
         const int sl = MODE == 0 ? s_slot[row_lo + lane] : p.slot_of_row[row_lo + lane];
         col = (MODE == 0 && !gather) ? kTerms * (sl / p.k) : kTerms * lane;
         if (MODE == 1) wt = p.scores[sl];
+      }
+      if (MODE == 0 && owner) {
+        // while the piece's MMAs run, the SwiGLU / term code once on made-up
+        // values (stores skipped), so that the real pass finds it cached
+        const bool ready = ptx::mbar_try_wait(accfull(ab), (pc / p.nacc) & 1);
+        if (!named_and(1, 128, ready))
+          h_terms(p, 0.f, 0.f, 0.f, 0.f, 0, 0, false, 0, 0, warp, lane, red, ntok > 4, true);
       }
       bool got = ptx::mbar_wait(accfull(ab), (pc / p.nacc) & 1, &abort_flag);
       for (int c2 = c_first; got && c2 < (int)blockIdx.x; ++c2)
