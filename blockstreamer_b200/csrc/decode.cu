@@ -36,16 +36,17 @@
 // holding its last stage, which adds the others' partial sums (written to
 // the workspace, counted by a flag per CTA) before its epilogue.
 //
-// One CTA per SM: warp 4 issues the TMA copies (weight tiles [128 rows x 256
-// codes] as stored, the B term rows, per-item scale blocks), warp 5 the MMAs,
-// warps 6-13 (two groups of four, one warp per 32-lane TMEM subpartition,
-// alternating stages) write every stage's scale factors into TMEM with
-// tcgen05.st, warps 0-3 drain the accumulators.  Measured on this GPU: one
-// thread issues a block-scaled MMA every ~115 cycles and a commit in ~90, so
-// the MMA thread's own instructions set the stage rate -- its loop has no
-// divisions and advances descriptors by addition -- and one group of
-// scale-factor warps (loads, TMEM stores and their wait: ~0.6 us a stage)
-// would be slower than the MMAs.
+// One CTA per SM, two pipelines that take alternate stages of every piece,
+// each with a TMA warp (weight tiles [128 rows x 256 codes] as stored, the B
+// term rows; pipeline 0's also the per-item scale blocks and B tiles), an MMA
+// thread, four scale-factor warps (one per 32-lane TMEM subpartition, writing
+// each stage's scale factors with tcgen05.st) and its own accumulator; warps
+// 0-3 add the two accumulators in the epilogue.  Measured on this GPU: one
+// thread issues a block-scaled MMA every ~115 cycles and a commit in ~90,
+// whatever other threads of the SM issue, so the issuing threads' own
+// instructions set the stage rate; two pipelines double it.  The loops have
+// no divisions and advance descriptors by addition.
+
 #include "bs_common.cuh"
 #include "bs_ptx.cuh"
 #include "bs_topk.cuh"
@@ -60,7 +61,9 @@ constexpr int kTerms = 4;       // e2m1 terms per activation
 constexpr int kRTok = 16;       // tokens per router CTA
 constexpr int kKC = 256;        // K elements per pipeline stage: 128 bytes of codes per row, 4 MMAs
 constexpr int kBM = 128;        // weight rows per item (MMA M)
-constexpr int kThreads = 448;   // warps 0-3 epilogue, 4 TMA, 5 MMA, 6-9 and 10-13 scale factors
+constexpr int kThreads = 384;   // warps 0-3 epilogue; pipeline 0: 4 TMA, 5 MMA, 6-7 scale factors; pipeline 1: 8-11
+constexpr int kAtomBytes = 2048; // a stage's scale factors as tcgen05.cp sources: SFA, SFB x 2 groups x 32 x 16 B
+constexpr int kSfWarps = 2;      // scale-factor warps a pipeline, each with one atom buffer
 constexpr int kTmemCols = 512;
 constexpr int kSfStageCols = 24;  // per stage: SFA 2 groups x 4 columns, SFB 2 groups x 4 or 8 columns
 constexpr int kMaxStages = 12;
@@ -308,7 +311,7 @@ __host__ __device__ inline MxSmem mx_smem(int K, int nb, int b_mode, int gp, int
   m.ring = al(m.ring_b + m.ring_sa + (b_mode == kBResident ? 0 : nb * gp));  // + B scale rows [nb][gp]
   m.res_b = b_mode == kBResident ? nkc * nb * 128 : 0;
   m.res = b_mode == kBResident ? al(m.res_b + nb * gp) : 0;
-  m.total = S * m.stage + nsc * m.ring + m.res + 1024;
+  m.total = 2 * kSfWarps * kAtomBytes + S * m.stage + nsc * m.ring + m.res + 1024;
   return m;
 }
 
@@ -510,7 +513,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
   // ring buffer b, bfree[b] that item's MMAs are done; accfull / accempty:
   // accumulator handoff; res: resident B landed; drain: teardown.  A waiter is
   // never two phases ahead of a barrier it waits on.
-  __shared__ uint64_t bars[3 * kMaxStages + 2 * kMaxRing + 6];
+  __shared__ uint64_t bars[3 * kMaxStages + 2 * kMaxRing + 6 + 2 * kSfWarps];
   __shared__ uint32_t tmem_holder;
   __shared__ volatile int abort_flag;
   __shared__ float red[2][4][4];
@@ -532,7 +535,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
   const int nkc = (K + kKC - 1) / kKC, nfull = K / kKC;
   const int nbk = nb > 128 ? 2 : 1;
   const MxSmem L = mx_smem(K, nb, p.b_mode, p.gp, S, NR);
-  uint8_t* ring0 = smem + S * L.stage;
+  // [scale-factor atoms | S stages | NR per-item buffers | resident B]; the
+  // atoms come first, so that every tcgen05.cp source lies well inside the
+  // allocation
+  uint8_t* atoms = smem;
+  uint8_t* stages = smem + 2 * kSfWarps * kAtomBytes;
+  uint8_t* ring0 = stages + S * L.stage;
   uint8_t* res = ring0 + NR * L.ring;
   auto data = [&](int s) { return ptx::smem_addr(bars + s); };
   auto empty = [&](int s) { return ptx::smem_addr(bars + kMaxStages + s); };
@@ -543,22 +551,24 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
   auto accempty = [&](int b) { return ptx::smem_addr(bars + 3 * kMaxStages + 2 * kMaxRing + 2 + b); };
   const uint32_t resb = ptx::smem_addr(bars + 3 * kMaxStages + 2 * kMaxRing + 4);
   const uint32_t drain = ptx::smem_addr(bars + 3 * kMaxStages + 2 * kMaxRing + 5);
+  auto atomfree = [&](int i) { return ptx::smem_addr(bars + 3 * kMaxStages + 2 * kMaxRing + 6 + i); };
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       ptx::mbar_init(data(s), 1);
       ptx::mbar_init(empty(s), 1);
-      ptx::mbar_init(sffull(s), 4);
+      ptx::mbar_init(sffull(s), 1);  // the commit of the stage's tcgen05.cp
     }
     for (int b = 0; b < NR; ++b) {
       ptx::mbar_init(itemb(b), 1);
-      ptx::mbar_init(bfree(b), 1);
+      ptx::mbar_init(bfree(b), 2);  // a commit from each pipeline's MMA thread
     }
     for (int b = 0; b < 2; ++b) {
-      ptx::mbar_init(accfull(b), 1);
+      ptx::mbar_init(accfull(b), 2);
       ptx::mbar_init(accempty(b), 4);
     }
     ptx::mbar_init(resb, 1);
-    ptx::mbar_init(drain, 1);
+    ptx::mbar_init(drain, 2);
+    for (int i = 0; i < 2 * kSfWarps; ++i) ptx::mbar_init(atomfree(i), 1);
     abort_flag = 0;
     ptx::fence_mbar_init();
   }
@@ -573,6 +583,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
   }
   pdl_wait();  // the logits / routing and the B operands come from the previous kernels
   pdl_launch();
+  __syncthreads();  // barriers initialized, tensor memory allocated
+  if (p.b_mode == kBResident && warp == 4 && lane == 0) {
+    // every token's B tiles and scale rows, once, while the routing runs
+    // (they do not depend on it); the TMA warp waits for them before it exits
+    const uint32_t rb = ptx::smem_addr(res);
+    ptx::mbar_arrive_expect_tx(resb, (uint32_t)(nkc * nb * 128 + kTerms * p.T * p.gp));
+    if (nfull > 0) ptx::tma_load_3d(rb, &pa.tm_b3, resb, 0, 0, 0);
+    if (nfull < nkc) ptx::tma_load_2d(rb + nfull * nb * 128, &pa.tm_b, resb, nfull * 128, 0);
+    ptx::bulk_load(rb + L.res_b, p.bsf, (uint32_t)(kTerms * p.T * p.gp), resb);
+  }
   if (MODE == 0) {
     // the stages' space is free until the pipeline starts
     route_dispatch(p, reinterpret_cast<int*>(smem), s_slot, s_grp, &s_ngrp, wsum);
@@ -614,8 +634,8 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
     q.kc1 = hi - s0 < nkc ? hi - s0 : nkc;
     return q;
   };
-  const uint32_t smem0 = ptx::smem_addr(smem);
-  const uint32_t sf_base = (uint32_t)(p.nacc * nb);  // TMEM column of stage 0's scale factors
+  const uint32_t smem0 = ptx::smem_addr(stages);
+  const uint32_t sf_base = (uint32_t)(2 * p.nacc * nb);  // TMEM column of stage 0's scale factors
 
   // MODE 0: the down projection's weights of the routed experts into L2 once
   // this CTA's own copies are issued (HBM would otherwise idle from the end
@@ -651,89 +671,113 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
   auto brow0 = [&](int2 gr) { return MODE == 0 ? 0 : gr.y * kTerms; };
   auto nbrows = [&](int2 gr) { return (MODE == 0 && !gather) ? kTerms * p.T : kTerms * (gr.x >> 16); };
 
-  if (warp == 4) {
-    // ---------------------------------------------------------- TMA producer (one warp)
+  // Two pipelines split every piece's stages (pipeline pl takes stages kc0 +
+  // pl, kc0 + pl + 2, ...): each has its own TMA warp, MMA thread, group of
+  // scale-factor warps, Sp stage slots and accumulator; the epilogue adds the
+  // two accumulators.  One thread issues a block-scaled MMA every ~115
+  // cycles whatever other threads of the SM issue, so two issuers double the
+  // tensor pipe's work per SM.
+  const int pl = warp >= 8 ? 1 : 0;
+  const int rw = warp >= 8 ? warp - 4 : warp;  // the warp's role in pipeline 0's numbering
+  const int Sp = S / 2;
+  if (rw == 4) {
+    // ---------------------------------------------------------- TMA producer (one warp a pipeline)
     // Lane 0 waits and issues the weight tiles; with gathered B, lane j
     // issues token j's boxes (one thread issuing 17 copies a stage was the
-    // limit at 64 tokens).
+    // limit at 64 tokens).  Pipeline 0's warp also loads the per-item blocks.
     const uint32_t full = 0xffffffffu;
-    int g = 0, n_issued = 0;
-    int s = 0, ph = 0;  // slot and parity of stage g: g % S, (g / S) & 1 (no divisions in the loop)
+    int g = 0, n_issued = 0;  // g: this pipeline's stages
+    int s = 0, ph = 0;        // their slot and parity: g % Sp, (g / Sp) & 1 (no divisions in the loop)
     bool ok = true;
-    if (lane == 0 && p.b_mode == kBResident && n_pc > 0) {
-      // every token's B tiles and scale rows, once
-      const uint32_t rb = ptx::smem_addr(res);
-      ptx::mbar_arrive_expect_tx(resb, (uint32_t)(nkc * nb * 128 + kTerms * p.T * p.gp));
-      if (nfull > 0) ptx::tma_load_3d(rb, &pa.tm_b3, resb, 0, 0, 0);
-      if (nfull < nkc) ptx::tma_load_2d(rb + nfull * nb * 128, &pa.tm_b, resb, nfull * 128, 0);
-      ptx::bulk_load(rb + L.res_b, p.bsf, (uint32_t)(kTerms * p.T * p.gp), resb);
-    }
+    // Per-item blocks (A scale rows, B scale rows, kBItem's B tiles) of piece
+    // pi, once its ring buffer is free (the MMAs of the piece NR earlier
+    // finished).  False on a timeout.  (Issuing the next piece's blocks
+    // during this piece's stages measured no faster.)
+    auto issue_items = [&](int pi) {
+      const int b = pi % NR;
+      bool fr = pi < NR;
+      if (!fr) {
+        if (lane == 0) fr = ptx::mbar_wait(bfree(b), ((pi / NR) - 1) & 1, &abort_flag);
+        fr = __shfl_sync(full, fr, 0);
+      }
+      if (!fr) return false;
+      const Piece qi = piece(pi);
+      const int2 gi = s_grp[qi.item / per_e];
+      const int ei = gi.x & 0xFFFF, ri = (qi.item % per_e) * kBM, nti = gi.x >> 16;
+      const int nri = min(kBM, Nw - ri), nbi = nbrows(gi), bi0 = brow0(gi);
+      const uint32_t sbt = ptx::smem_addr(ring0 + b * L.ring), sca = sbt + L.ring_b, scb = sca + L.ring_sa;
+      if (lane == 0) {
+        // the item's scale rows (A contiguous [rows][G], B [nbv][gp]) and, per
+        // item, its B tiles for all of K
+        uint32_t tx = nri * G;
+        if (p.b_mode != kBResident) tx += nbi * p.gp;
+        if (p.b_mode == kBItem) tx += nkc * nb * 128;
+        ptx::mbar_arrive_expect_tx(itemb(b), tx);
+        ptx::bulk_load(sca, p.scales + ((int64_t)ei * Nw + ri) * G, (uint32_t)(nri * G), itemb(b));
+        if (!gather && p.b_mode != kBResident)
+          ptx::bulk_load(scb, p.bsf + (int64_t)bi0 * p.gp, (uint32_t)(nbi * p.gp), itemb(b));
+        if (p.b_mode == kBItem) {
+          if (nfull > 0) ptx::tma_load_3d(sbt, &pa.tm_b3, itemb(b), 0, bi0, 0);
+          if (nfull < nkc) ptx::tma_load_2d(sbt + nfull * nb * 128, &pa.tm_b, itemb(b), nfull * 128, bi0);
+        }
+      }
+      __syncwarp();
+      if (gather && lane < nti) {
+        const int tr = (s_slot[gi.y + lane] / p.k) * kTerms;  // the lane's token: its first term row
+        ptx::bulk_load(scb + lane * kTerms * p.gp, p.bsf + (int64_t)tr * p.gp, (uint32_t)(kTerms * p.gp), itemb(b));
+      }
+      ++n_issued;
+      return true;
+    };
     for (int pc = 0; pc < n_pc && ok; ++pc) {
       const Piece q = piece(pc);
       const int item = q.item;
       const int2 gr = s_grp[item / per_e];
       const int e = gr.x & 0xFFFF, r0 = (item % per_e) * kBM, ntok = gr.x >> 16;
       const int nrows = min(kBM, Nw - r0), nbv = nbrows(gr), b0 = brow0(gr);
-      const int b = pc % NR;
-      bool w = true;
-      if (lane == 0 && pc >= NR) w = ptx::mbar_wait(bfree(b), ((pc / NR) - 1) & 1, &abort_flag);
-      if (!__shfl_sync(full, w, 0)) break;
-      const uint32_t sbt = ptx::smem_addr(ring0 + b * L.ring), sca = sbt + L.ring_b, scb = sca + L.ring_sa;
       // gathered B: this lane's token (its first term row)
       const int trow = (gather && lane < ntok) ? (s_slot[gr.y + lane] / p.k) * kTerms : 0;
-      if (lane == 0) {
-        // the item's scale rows (A contiguous [rows][G], B [nbv][gp]) and, per
-        // item, its B tiles for all of K
-        uint32_t tx = nrows * G;
-        if (p.b_mode != kBResident) tx += nbv * p.gp;
-        if (p.b_mode == kBItem) tx += nkc * nb * 128;
-        ptx::mbar_arrive_expect_tx(itemb(b), tx);
-        ptx::bulk_load(sca, p.scales + ((int64_t)e * Nw + r0) * G, (uint32_t)(nrows * G), itemb(b));
-        if (!gather && p.b_mode != kBResident)
-          ptx::bulk_load(scb, p.bsf + (int64_t)b0 * p.gp, (uint32_t)(nbv * p.gp), itemb(b));
-        if (p.b_mode == kBItem) {
-          if (nfull > 0) ptx::tma_load_3d(sbt, &pa.tm_b3, itemb(b), 0, b0, 0);
-          if (nfull < nkc) ptx::tma_load_2d(sbt + nfull * nb * 128, &pa.tm_b, itemb(b), nfull * 128, b0);
-        }
-      }
-      __syncwarp();
-      if (gather && lane < ntok)
-        ptx::bulk_load(scb + lane * kTerms * p.gp, p.bsf + (int64_t)trow * p.gp, (uint32_t)(kTerms * p.gp),
-                       itemb(b));
-      ++n_issued;
-      for (int kc = q.kc0; kc < q.kc1; ++kc, ++g) {
-        if (lane == 0 && g >= S) w = ptx::mbar_wait(empty(s), ph ^ 1, &abort_flag);
+      bool w = true;
+      // pipeline 0: this piece's per-item blocks, once their buffer is free
+      if (pl == 0 && !issue_items(pc)) break;
+      for (int kc = q.kc0 + pl; kc < q.kc1; kc += 2, ++g) {
+        const int sl = pl * Sp + s;
+        if (lane == 0 && g >= Sp) w = ptx::mbar_wait(empty(sl), ph ^ 1, &abort_flag);
         if (!__shfl_sync(full, w, 0)) {
           ok = false;
           break;
         }
-        const uint32_t sa = smem0 + s * L.stage;
+        const uint32_t sa = smem0 + sl * L.stage;
         if (lane == 0) {
-          ptx::mbar_arrive_expect_tx(data(s), (uint32_t)(gather ? kBM * 128 + nbv * 128 : L.stage));
-          ptx::tma_load_2d(sa, &pa.tm_a, data(s), kc * 128, e * Nw + r0);
-          if (p.b_mode == kBStage) ptx::tma_load_2d(sa + kBM * 128, &pa.tm_b, data(s), kc * 128, b0);
+          ptx::mbar_arrive_expect_tx(data(sl), (uint32_t)(gather ? kBM * 128 + nbv * 128 : L.stage));
+          ptx::tma_load_2d(sa, &pa.tm_a, data(sl), kc * 128, e * Nw + r0);
+          if (p.b_mode == kBStage) ptx::tma_load_2d(sa + kBM * 128, &pa.tm_b, data(sl), kc * 128, b0);
         }
         __syncwarp();
         // one 4-row box per token of the group (the stage's count covers exactly these)
         if (gather && lane < ntok)
-          ptx::tma_load_2d(sa + kBM * 128 + lane * kTerms * 128, &pa.tm_b, data(s), kc * 128, trow);
-        if (++s == S) s = 0, ph ^= 1;
+          ptx::tma_load_2d(sa + kBM * 128 + lane * kTerms * 128, &pa.tm_b, data(sl), kc * 128, trow);
+        if (++s == Sp) s = 0, ph ^= 1;
       }
     }
     if (lane == 0 && abort_flag) {
-      // after a timeout elsewhere: let this CTA's copies in flight land
-      // (bounded) before it exits
+      // after a timeout elsewhere: let this warp's copies in flight land
+      // (bounded) before the CTA exits
       volatile int quiet = 0;
-      for (int gg = max(0, g - S); gg < g; ++gg)
-        ptx::mbar_wait(data(gg % S), (gg / S) & 1, &quiet, 100000000LL);
+      for (int gg = max(0, g - Sp); gg < g; ++gg)
+        ptx::mbar_wait(data(pl * Sp + gg % Sp), (gg / Sp) & 1, &quiet, 100000000LL);
       for (int i2 = max(0, n_issued - NR); i2 < n_issued; ++i2)
         ptx::mbar_wait(itemb(i2 % NR), (i2 / NR) & 1, &quiet, 100000000LL);
-      if (p.b_mode == kBResident && n_pc > 0) ptx::mbar_wait(resb, 0, &quiet, 100000000LL);
+    }
+    if (pl == 0 && lane == 0 && p.b_mode == kBResident) {
+      // the resident B copies must have landed before the CTA exits (bounded)
+      volatile int quiet = 0;
+      ptx::mbar_wait(resb, 0, &quiet, 100000000LL);
     }
     __syncwarp();
-    if (!abort_flag) prefetch_next();
-  } else if (warp == 5) {
-    // ---------------------------------------------------------- MMA issue (one thread)
+    if (pl == 0 && !abort_flag) prefetch_next();
+  } else if (rw == 5) {
+    // ---------------------------------------------------------- MMA issue (one thread a pipeline)
     if (lane == 0) {
       // one thread whose per-stage instructions are the issue rate: no
       // divisions in the loop, descriptors advanced by addition
@@ -748,7 +792,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
         if (pc >= p.nacc && !ptx::mbar_wait(accempty(ab), ((pc / p.nacc) - 1) & 1, &abort_flag)) break;
         if (p.b_mode == kBItem && !ptx::mbar_wait(itemb(b), (pc / NR) & 1, &abort_flag)) break;
         ptx::tc_fence_after();
-        const uint32_t acc = tmem + ab * nb;
+        const uint32_t acc = tmem + (pl * p.nacc + ab) * nb;
         const uint32_t bt = p.b_mode == kBItem ? ptx::smem_addr(ring0 + b * L.ring) : ptx::smem_addr(res);
         const uint32_t id0 = ptx::idesc_mxf4(N, 0, 0), id2 = ptx::idesc_mxf4(N, 2, 2);
         const bool b_in_stage = p.b_mode == kBStage || gather;
@@ -756,43 +800,50 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
         // descriptor by a 16-byte multiple adds to it
         const uint64_t ad0 = ptx::sdesc_kmajor_sw128(smem0);
         const uint64_t bd_item = ptx::sdesc_kmajor_sw128(bt) + (uint64_t)((q.kc0 * nb * 128) >> 4);
-        for (int kc = q.kc0; kc < q.kc1; ++kc, ++g) {
-          if (!ptx::mbar_wait(data(s), ph, &abort_flag) || !ptx::mbar_wait(sffull(s), ph, &abort_flag)) {
+        for (int kc = q.kc0 + pl; kc < q.kc1; kc += 2, ++g) {
+          const int sl = pl * Sp + s;
+          if (!ptx::mbar_wait(data(sl), ph, &abort_flag) || !ptx::mbar_wait(sffull(sl), ph, &abort_flag)) {
             ok = false;
             break;
           }
           ptx::tc_fence_after();
-          const uint64_t ad = ad0 + (uint64_t)((s * L.stage) >> 4);
+          const uint64_t ad = ad0 + (uint64_t)((sl * L.stage) >> 4);
           const uint64_t bd = b_in_stage ? ad + (kBM * 128 >> 4) : bd_item + (uint64_t)(((kc - q.kc0) * nb * 128) >> 4);
-          // scale factors (written by warps 6-9): SFA at columns 4q, SFB at
-          // 8 + 4 nbk q for groups q = 0, 1 of four k-blocks
-          const uint32_t sf = tmem + sf_base + s * kSfStageCols;
+          // scale factors (written by the pipeline's scale-factor warps): SFA
+          // at columns 4q, SFB at 8 + 4 nbk q for groups q = 0, 1 of four k-blocks
+          const uint32_t sf = tmem + sf_base + sl * kSfStageCols;
           const int nm = (K - kc * kKC) >= kKC ? 4 : (K - kc * kKC) / 64;
-          const bool acc0 = kc != q.kc0;
+          const bool acc0 = kc != q.kc0 + pl;  // this pipeline's first stage of the piece
           ptx::mma_mxf4_ss(acc, ad, bd, id0, sf, sf + 8, acc0);
           if (nm > 1) ptx::mma_mxf4_ss(acc, ad + 2, bd + 2, id2, sf, sf + 8, 1);
           if (nm > 2) ptx::mma_mxf4_ss(acc, ad + 4, bd + 4, id0, sf + 4, sf + 8 + 4 * nbk, 1);
           if (nm > 3) ptx::mma_mxf4_ss(acc, ad + 6, bd + 6, id2, sf + 4, sf + 8 + 4 * nbk, 1);
-          ptx::tc_commit(empty(s));
-          if (++s == S) s = 0, ph ^= 1;
+          ptx::tc_commit(empty(sl));
+          if (++s == Sp) s = 0, ph ^= 1;
         }
-        if (ok) {
+        if (ok) {  // both pipelines arrive (a commit with no MMAs of this piece arrives once earlier ones finish)
           ptx::tc_commit(accfull(ab));
           ptx::tc_commit(bfree(b));
         }
       }
     }
     __syncwarp();
-  } else if (warp >= 6) {
+  } else if (rw >= 6) {
     // ---------------------------------------------------------- scale factors into TMEM
-    // This warp writes its own 32-lane subpartition; the four hold copies.
-    // SFA word (q, j) of lane l: scales of row l + 32 j, k-blocks 4q..4q+3;
-    // SFB word (q, j): B row l + 32 j.
-    // Two groups of four (warps 6-9: even stages, 10-13: odd stages): one
-    // stage's loads, TMEM stores and their wait take longer than its MMAs.
-    const uint32_t lanes = (uint32_t)(32 * (warp & 3)) << 16;
-    const int grp = warp >= 10;
-    int g = 0, s = 0, ph = 0;  // stage g's slot and parity
+    // kSfWarps warps a pipeline take its stages in turn.  A warp lays out a
+    // stage's scale factors in shared memory as 32 rows of 16 bytes -- row l
+    // holds the words of rows l + 32 j, j = 0..3, each word four k-blocks'
+    // scales; SFA then SFB, k-block groups q = 0, 1 -- and lane 0 copies each
+    // 512-byte block into the stage's four columns of all four TMEM
+    // subpartitions (tcgen05.cp ... warpx4).  The commit of the copies
+    // completes sffull (for the MMA thread) and atomfree (the warp's own
+    // buffer may be rewritten); nothing waits on the TMEM writes themselves.
+    const int sw = rw - 6;
+    const uint32_t atom_s = ptx::smem_addr(atoms + (pl * kSfWarps + sw) * kAtomBytes);
+    uint8_t* atom = atoms + (pl * kSfWarps + sw) * kAtomBytes;
+    const uint32_t afree = atomfree(pl * kSfWarps + sw);
+    int g = 0, s = 0, ph = 0;  // this pipeline's stage g: slot and parity
+    int used = 0;              // stages this warp laid out
     bool ok = true;
     if (p.b_mode == kBResident && n_pc > 0) {
       bool w = true;
@@ -810,55 +861,64 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
       if (!__shfl_sync(0xffffffffu, w, 0)) break;
       const uint8_t* sca = ring0 + b * L.ring + L.ring_b;
       const uint8_t* scb = p.b_mode == kBResident ? res + L.res_b : sca + L.ring_sa;
-      for (int kc = q.kc0; kc < q.kc1; ++kc, ++g) {
-        if ((g & 1) != grp) {
-          if (++s == S) s = 0, ph ^= 1;
-          continue;
-        }
-        if (g >= S) {
-          if (lane == 0) w = ptx::mbar_wait(empty(s), ph ^ 1, &abort_flag);
+      for (int kc = q.kc0 + pl; kc < q.kc1; kc += 2, ++g) {
+        const int sl = pl * Sp + s;
+        if ((g & (kSfWarps - 1)) == sw) {
+          // the slot's columns are free once the MMAs of its previous stage
+          // finished; this warp's buffer once its previous copies finished
+          if (lane == 0 && g >= Sp) w = ptx::mbar_wait(empty(sl), ph ^ 1, &abort_flag);
+          if (lane == 0 && w && used > 0) w = ptx::mbar_wait(afree, (used - 1) & 1, &abort_flag);
           if (!__shfl_sync(0xffffffffu, w, 0)) {
             ok = false;
             break;
           }
-        }
-        uint32_t wa[8], wb[16];
+          uint32_t wa[8], wb[8];
 #pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          const int gq = 2 * kc + q;
-          const bool gv = 4 * gq < G;
+          for (int qq = 0; qq < 2; ++qq) {
+            const int gq = 2 * kc + qq;
+            const bool gv = 4 * gq < G;
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int r = lane + 32 * j;
-            uint32_t v = 0;
-            if (gv && r < nrows) {
-              const uint16_t* row = reinterpret_cast<const uint16_t*>(sca + r * G);
-              v = row[2 * gq] | ((4 * gq + 2 < G) ? (uint32_t)row[2 * gq + 1] << 16 : 0u);
-            }
-            wa[4 * q + j] = v;
-          }
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            const int r = lane + 32 * j;
-            const uint32_t u = (gv && j < 4 * nbk && r < nbv) ? *reinterpret_cast<const uint32_t*>(scb + r * p.gp + 4 * gq) : 0u;
-            if (nbk == 1) {
-              if (j < 4) wb[4 * q + j] = u;
-            } else {
-              wb[8 * q + j] = u;
+            for (int j = 0; j < 4; ++j) {
+              const int r = lane + 32 * j;
+              uint32_t v = 0;
+              if (gv && r < nrows) {
+                const uint16_t* row = reinterpret_cast<const uint16_t*>(sca + r * G);
+                v = row[2 * gq] | ((4 * gq + 2 < G) ? (uint32_t)row[2 * gq + 1] << 16 : 0u);
+              }
+              wa[4 * qq + j] = v;
+              wb[4 * qq + j] = (gv && r < nbv) ? *reinterpret_cast<const uint32_t*>(scb + r * p.gp + 4 * gq) : 0u;
             }
           }
+#pragma unroll
+          for (int qq = 0; qq < 2; ++qq) {
+            *reinterpret_cast<uint4*>(atom + qq * 512 + lane * 16) = make_uint4(wa[4 * qq], wa[4 * qq + 1], wa[4 * qq + 2], wa[4 * qq + 3]);
+            *reinterpret_cast<uint4*>(atom + 1024 + qq * 512 + lane * 16) =
+                make_uint4(wb[4 * qq], wb[4 * qq + 1], wb[4 * qq + 2], wb[4 * qq + 3]);
+          }
+          ptx::fence_proxy_async_smem();  // the rows, written by this warp, to the copy's (async) reads
+          __syncwarp();
+          if (lane == 0) {
+            ptx::tc_fence_after();
+            // columns: SFA group q at 4 q, SFB group q at 8 + 4 q (one 128-row block of B)
+            const uint32_t sf = tmem + sf_base + sl * kSfStageCols;
+#pragma unroll
+            for (int c4 = 0; c4 < 4; ++c4)
+              ptx::tc_cp_32x128b_warpx4(sf + 4 * c4, ptx::sdesc_rows16(atom_s + 512 * c4));
+            ptx::tc_commit(sffull(sl));
+            ptx::tc_commit(afree);
+          }
+          __syncwarp();
+          ++used;
         }
-        const uint32_t sf = tmem + lanes + sf_base + s * kSfStageCols;
-        ptx::tmem_st_32x32b_x8(sf, wa);
-        if (nbk == 1) ptx::tmem_st_32x32b_x8(sf + 8, wb);
-        else ptx::tmem_st_32x32b_x16(sf + 8, wb);
-        ptx::tmem_wait_st();
-        ptx::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(sffull(s));
-        if (++s == S) s = 0, ph ^= 1;
+        if (++s == Sp) s = 0, ph ^= 1;
       }
     }
+    if (lane == 0 && used > 0) {
+      // copies still in flight must finish before the tensor memory is freed (bounded)
+      volatile int quiet = 0;
+      ptx::mbar_wait(afree, (used - 1) & 1, &quiet, 100000000LL);
+    }
+    __syncwarp();
   } else {
     // ---------------------------------------------------------- epilogue
     const uint32_t lanes = (uint32_t)(32 * warp) << 16;
@@ -902,7 +962,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
         if (nonempty(c2)) got = wait_flag(p.flags + c2, 4u, &abort_flag);
       if (!named_and(1, 128, got)) break;
       ptx::tc_fence_after();
-      const uint32_t tl = tmem + lanes + ab * nb;
+      const uint32_t tl = tmem + lanes + ab * nb;     // pipeline 0's accumulator
+      const uint32_t tl1 = tl + p.nacc * nb;           // pipeline 1's, written if the piece has two stages
+      const bool two = q.kc1 - q.kc0 >= 2;
       const int nchunk = (ntok + 3) / 4;
       for (int c = 0; c < nchunk; ++c) {
         // the head pieces' sums of these four tokens: all loads in flight at once
@@ -916,11 +978,12 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
           const int cj = __shfl_sync(0xffffffffu, col, (c * 4 + jj) & 31);
-          uint32_t u[4];
+          uint32_t u[4], v[4] = {0u, 0u, 0u, 0u};
           ptx::tmem_ld_32x32b_x4(tl + cj, u);  // tokens past ntok read column 0, unused
+          if (two) ptx::tmem_ld_32x32b_x4(tl1 + cj, v);
           ptx::tmem_wait_ld();
-          acc[jj] += __uint_as_float(u[0]) + __uint_as_float(u[1]) + __uint_as_float(u[2]) +
-                     __uint_as_float(u[3]) + bv;
+          acc[jj] += ((__uint_as_float(u[0]) + __uint_as_float(u[1])) + (__uint_as_float(u[2]) + __uint_as_float(u[3]))) +
+                     ((__uint_as_float(v[0]) + __uint_as_float(v[1])) + (__uint_as_float(v[2]) + __uint_as_float(v[3]))) + bv;
         }
         if (c == nchunk - 1) {
           // accumulator drained: the MMAs of a later item may use it
@@ -955,12 +1018,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
     }
   }
   __syncthreads();
+  // MMAs may still be in flight after a timeout: both MMA threads commit to
+  // `drain`, whose completion warp 5 waits for (bounded) before the tensor
+  // memory is released
+  if ((warp == 5 || warp == 9) && lane == 0 && abort_flag) ptx::tc_commit(drain);
   if (warp == 5) {
     if (lane == 0 && abort_flag) {
-      // MMAs may still be in flight after a timeout: let them finish (bounded)
-      // before the tensor memory is released.
       record_status(p.status, BS_ERR_TIMEOUT);
-      ptx::tc_commit(drain);
       volatile int quiet = 0;
       ptx::mbar_wait(drain, 0, &quiet, 100000000LL);
     }
@@ -1025,7 +1089,8 @@ int plan_mx(MxArgs& a, std::initializer_list<int> modes) {
   const int budget = 198 * 1024;  // dynamic shared memory (the static arrays take ~18 KB)
   a.stages = 0;
   for (int b_mode : modes) {
-    for (int S = kMaxStages; S >= ((b_mode == kBStage || b_mode == kBGather) ? 2 : 4); --S) {
+    // an even count: the two pipelines hold half each
+    for (int S = kMaxStages; S >= ((b_mode == kBStage || b_mode == kBGather) ? 2 : 4); S -= 2) {
       const int nsc = 2;
       if (mx_smem(a.K, a.nb, b_mode, a.gp, S, nsc).total <= budget) {
         a.b_mode = b_mode, a.stages = S, a.nsc = nsc;
@@ -1035,8 +1100,11 @@ int plan_mx(MxArgs& a, std::initializer_list<int> modes) {
     if (a.stages) break;
   }
   BS_REQUIRE(a.stages >= 2, BS_ERR_UNSUPPORTED, "decode path: B tile of %d rows does not fit", a.nb);
-  a.nacc = (2 * a.nb + a.stages * kSfStageCols <= kTmemCols) ? 2 : 1;
-  BS_REQUIRE(a.nacc * a.nb + a.stages * kSfStageCols <= kTmemCols, BS_ERR_UNSUPPORTED,
+  // one 128-row block of B scale factors per k-block group (the tcgen05.cp layout)
+  BS_REQUIRE(a.nb <= 128, BS_ERR_UNSUPPORTED, "decode path: B tile of %d rows", a.nb);
+  // accumulators: two pipelines x (two buffers if they fit, else one)
+  a.nacc = (4 * a.nb + a.stages * kSfStageCols <= kTmemCols) ? 2 : 1;
+  BS_REQUIRE(2 * a.nacc * a.nb + a.stages * kSfStageCols <= kTmemCols, BS_ERR_UNSUPPORTED,
              "decode path: tensor memory plan does not fit");
   return BS_OK;
 }
