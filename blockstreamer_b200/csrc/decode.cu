@@ -345,8 +345,22 @@ __device__ void route_dispatch(const MxArgs& p, int* scratch, int* s_slot, int2*
       const float* row = lg + t * E;
       const float v = row[e];
       int r = 0;
+      if ((E & 3) == 0) {
+        const float4* row4 = reinterpret_cast<const float4*>(row);
+        int r1 = 0, r2 = 0, r3 = 0;
 #pragma unroll 8
-      for (int e2 = 0; e2 < E; ++e2) r += (row[e2] > v) | ((row[e2] == v) & (e2 < e));
+        for (int e4 = 0; e4 < E / 4; ++e4) {
+          const float4 w = row4[e4];
+          const int b2 = 4 * e4;
+          r += (w.x > v) | ((w.x == v) & (b2 < e));
+          r1 += (w.y > v) | ((w.y == v) & (b2 + 1 < e));
+          r2 += (w.z > v) | ((w.z == v) & (b2 + 2 < e));
+          r3 += (w.w > v) | ((w.w == v) & (b2 + 3 < e));
+        }
+        r += r1 + r2 + r3;
+      } else {
+        for (int e2 = 0; e2 < E; ++e2) r += (row[e2] > v) | ((row[e2] == v) & (e2 < e));
+      }
       if (r < k) {
         s_idx[t * k + r] = e;
         sv[t * k + r] = v;
@@ -367,6 +381,60 @@ __device__ void route_dispatch(const MxArgs& p, int* scratch, int* s_slot, int2*
                     writer ? p.scores + (int64_t)t * k : nullptr, s_idx + t * k);
   } else {
     for (int i = tid; i < n; i += kThreads) s_idx[i] = p.idx[i];
+  }
+  if (n <= 32 && T <= kGroupTok) {
+    // Few slots: one warp dispatches them (every expert then has <= T <=
+    // kGroupTok tokens, one group).  Slot j's row: the valid slots with a
+    // lower expert, or the same expert and a lower slot index; its group: the
+    // distinct experts below.  Same tables as the general path below.
+    __syncthreads();  // s_idx complete
+    int* lead = scratch + n;  // [n]: slot j is its expert's first slot (cnt's space and, past E, the rank scratch, both unused now)
+    if (warp == 0) {
+      const int e = lane < n ? s_idx[lane] : -1;
+      const bool valid = lane < n && e >= 0 && e < E;
+      if (lane < n && writer && p.logits) p.idx[lane] = e;
+      if (lane < n && !valid && writer) record_status(p.status, BS_ERR_INVALID_ARGUMENT);
+      int below = 0, same = 0, same_before = 0;
+      for (int j = 0; j < n; ++j) {
+        const int ej = s_idx[j];
+        const bool vj = ej >= 0 && ej < E;
+        below += vj && ej < e;
+        same += vj && ej == e;
+        same_before += vj && ej == e && j < lane;
+      }
+      const bool first = valid && same_before == 0;
+      if (lane < n) lead[lane] = first;
+      __syncwarp();
+      int grank = 0;
+      for (int j = 0; j < n; ++j) grank += lead[j] && s_idx[j] < e;
+      const int pos = below + same_before;
+      if (first) {
+        const int2 gr = make_int2(e | (same << 16), below);
+        s_grp[grank] = gr;
+        if (writer) p.groups[grank] = gr;
+      }
+      if (valid) s_slot[pos] = lane;
+      if (writer && lane < n) {
+        p.row_of_slot[lane] = valid ? pos : -1;
+        if (valid) p.slot_of_row[pos] = lane;
+      }
+      const int ng = __popc(__ballot_sync(0xffffffffu, first));
+      if (lane == 0) {
+        *s_ngrp = ng;
+        if (writer) p.meta->n_groups = ng;
+      }
+    }
+    if (writer)  // first row of every expert (and the total)
+      for (int e = tid; e <= E; e += kThreads) {
+        int r = 0;
+        for (int j = 0; j < n; ++j) {
+          const int ej = s_idx[j];
+          r += ej >= 0 && ej < E && ej < e;
+        }
+        p.offsets[e] = r;
+      }
+    __syncthreads();
+    return;
   }
   for (int e = tid; e < E; e += kThreads) cnt[e] = 0;
   __syncthreads();
