@@ -61,7 +61,7 @@ constexpr int kTerms = 4;       // e2m1 terms per activation
 constexpr int kRTok = 16;       // tokens per router CTA
 constexpr int kKC = 256;        // K elements per pipeline stage: 128 bytes of codes per row, 4 MMAs
 constexpr int kBM = 128;        // weight rows per item (MMA M)
-constexpr int kThreads = 384;   // warps 0-3 epilogue; pipeline 0: 4 TMA, 5 MMA, 6-7 scale factors; pipeline 1: 8-11
+constexpr int kThreads = 512;   // pipeline 0: warps 4 TMA, 5 MMA, 6-7 scale factors; pipeline 1: 8-11; epilogues 0-3, 12-15
 constexpr int kAtomBytes = 2048; // a stage's scale factors as tcgen05.cp sources: SFA, SFB x 2 groups x 32 x 16 B
 constexpr int kSfWarps = 2;      // scale-factor warps a pipeline, each with one atom buffer
 constexpr int kTmemCols = 512;
@@ -520,7 +520,7 @@ __device__ void route_dispatch(const MxArgs& p, int* scratch, int* s_slot, int2*
 // that the real pass does not fetch its instructions while HBM is saturated
 // (a few microseconds otherwise).  Out of line: one copy serves both.
 __device__ __noinline__ void h_terms(const MxArgs& p, float a0, float a1, float a2, float a3, int c, int ntok,
-                                     bool rv, int row_lo, int i, int warp, int lane, float (*red)[4][4],
+                                     bool rv, int row_lo, int i, int ew, int lane, float (*red)[8][4],
                                      bool unrolled, bool dry) {
   const float acc[4] = {a0, a1, a2, a3};
   float r[4];
@@ -538,13 +538,13 @@ __device__ __noinline__ void h_terms(const MxArgs& p, float a0, float a1, float 
 #pragma unroll
     for (int jj = 0; jj < 4; ++jj) {
       const float m = group_max<32>(fabsf(r[jj]));
-      if (lane == 0) red[term & 1][warp][jj] = m;
+      if (lane == 0) red[term & 1][ew][jj] = m;
     }
-    named_sync(2 + (warp >> 1), 64);  // a 32-block of h: warps (0, 1) or (2, 3)
+    named_sync(2 + (ew >> 1), 64);  // a 32-block of h: the group's subpartitions (0, 1) or (2, 3)
 #pragma unroll
     for (int jj = 0; jj < 4; ++jj) {
       const int tok = c * 4 + jj;
-      const uint32_t sb = e8m0_for_max(fmaxf(red[term & 1][warp][jj], red[term & 1][warp ^ 1][jj]));
+      const uint32_t sb = e8m0_for_max(fmaxf(red[term & 1][ew][jj], red[term & 1][ew ^ 1][jj]));
       const float q = r[jj] * exp2_neg(sb);
       const float qn = __shfl_down_sync(0xffffffffu, q, 2);  // h_{i+1}
       const uint32_t byte = ptx::e2m1x2_from_f32(q, qn);
@@ -552,7 +552,7 @@ __device__ __noinline__ void h_terms(const MxArgs& p, float a0, float a1, float 
       if (tok < ntok && rv && !dry) {
         const int64_t hr = (int64_t)(row_lo + tok) * kTerms + term;
         if ((lane & 3) == 0) p.hq[hr * (I / 2) + (i >> 1)] = (uint8_t)byte;
-        if (lane == 0 && !(warp & 1)) p.hs[hr * p.gp_out + (i >> 5)] = (uint8_t)sb;
+        if (lane == 0 && !(ew & 1)) p.hs[hr * p.gp_out + (i >> 5)] = (uint8_t)sb;
       }
     }
   };
@@ -584,7 +584,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
   __shared__ uint64_t bars[3 * kMaxStages + 2 * kMaxRing + 6 + 2 * kSfWarps];
   __shared__ uint32_t tmem_holder;
   __shared__ volatile int abort_flag;
-  __shared__ float red[2][4][4];
+  __shared__ float red[2][8][4];
   __shared__ int2 s_grp[kMaxGroups];  // (expert | tokens << 16, first row)
   __shared__ int s_ngrp;
   __shared__ int s_slot[MODE == 0 ? kMaxDecodeT * 32 : 1];  // MODE 0: slot of each dispatch row
@@ -745,8 +745,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
   // two accumulators.  One thread issues a block-scaled MMA every ~115
   // cycles whatever other threads of the SM issue, so two issuers double the
   // tensor pipe's work per SM.
-  const int pl = warp >= 8 ? 1 : 0;
-  const int rw = warp >= 8 ? warp - 4 : warp;  // the warp's role in pipeline 0's numbering
+  const int pl = (warp >= 8 && warp < 12) ? 1 : 0;
+  // the warp's role in pipeline 0's numbering; 0-3: epilogue (both groups)
+  const int rw = (warp >= 8 && warp < 12) ? warp - 4 : (warp >= 12 ? warp - 12 : warp);
   const int Sp = S / 2;
   if (rw == 4) {
     // ---------------------------------------------------------- TMA producer (one warp a pipeline)
@@ -989,16 +990,22 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
     __syncwarp();
   } else {
     // ---------------------------------------------------------- epilogue
-    const uint32_t lanes = (uint32_t)(32 * warp) << 16;
+    // Two groups of four warps (one per TMEM subpartition each), group eg
+    // draining accumulator buffer eg: pieces alternate between them, so two
+    // epilogues run at once (at a few tokens one epilogue outlasts a piece's
+    // MMAs).  With a single buffer group 1 has nothing to do.
+    const int eg = warp >= 12 ? 1 : 0, ew = eg * 4 + (warp & 3);
+    const int ebar = eg ? 6 : 1;  // the group's named barrier (h_terms' pairs use 2-5)
+    const uint32_t lanes = (uint32_t)(32 * (warp & 3)) << 16;
     bool ok = true;
-    for (int pc = 0; pc < n_pc && ok; ++pc) {
+    for (int pc = eg; pc < n_pc && ok && eg < p.nacc; pc += p.nacc) {
       const Piece q = piece(pc);
       const int item = q.item;
       const int2 gr = s_grp[item / per_e];
       const int e = gr.x & 0xFFFF, ntok = gr.x >> 16, row_lo = gr.y, r0 = (item % per_e) * kBM;
       const int nrows = min(kBM, Nw - r0);
       const int ab = pc % p.nacc;
-      const int lrow = 32 * warp + lane;
+      const int lrow = 32 * (warp & 3) + lane;
       const bool rv = lrow < nrows;
       const int64_t grow = (int64_t)e * Nw + r0 + lrow;
       // a head piece of a split item leaves its sums to the item's tail piece
@@ -1022,13 +1029,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
         // while the piece's MMAs run, the SwiGLU / term code once on made-up
         // values (stores skipped), so that the real pass finds it cached
         const bool ready = ptx::mbar_try_wait(accfull(ab), (pc / p.nacc) & 1);
-        if (!named_and(1, 128, ready))
-          h_terms(p, 0.f, 0.f, 0.f, 0.f, 0, 0, false, 0, 0, warp, lane, red, ntok > 4, true);
+        if (!named_and(ebar, 128, ready))
+          h_terms(p, 0.f, 0.f, 0.f, 0.f, 0, 0, false, 0, 0, ew, lane, red, ntok > 4, true);
       }
       bool got = ptx::mbar_wait(accfull(ab), (pc / p.nacc) & 1, &abort_flag);
       for (int c2 = c_first; got && c2 < (int)blockIdx.x; ++c2)
         if (nonempty(c2)) got = wait_flag(p.flags + c2, 4u, &abort_flag);
-      if (!named_and(1, 128, got)) break;
+      if (!named_and(ebar, 128, got)) break;
       ptx::tc_fence_after();
       const uint32_t tl = tmem + lanes + ab * nb;     // pipeline 0's accumulator
       const uint32_t tl1 = tl + p.nacc * nb;           // pipeline 1's, written if the piece has two stages
@@ -1073,7 +1080,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
             if (tok < ntok && rv) p.y[(int64_t)(row_lo + tok) * Nw + r0 + lrow] = acc[jj] * w;
           }
         } else {
-          h_terms(p, acc[0], acc[1], acc[2], acc[3], c, ntok, rv, row_lo, (r0 + lrow) >> 1, warp, lane, red,
+          h_terms(p, acc[0], acc[1], acc[2], acc[3], c, ntok, rv, row_lo, (r0 + lrow) >> 1, ew, lane, red,
                   nchunk > 1, false);
         }
       }
