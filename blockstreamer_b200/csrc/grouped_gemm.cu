@@ -15,11 +15,13 @@
 //   * B (tokens): 128B-swizzled TMA tiles of 64 x 64 bf16 in shared memory.
 //   * D: fp32 accumulators in TMEM (up to 320 columns: one 128x256 and one
 //     128x64 MMA per K16 step), drained by four epilogue warps with tcgen05.ld.
-// Warp roles (480 threads): 0 token-tile TMA producer, 1 MMA issuer (+TMEM
-// owner), 2-5 epilogue, 6-13 dequant, 14 weight TMA producer.  The MMA issuer
-// is the critical path (each tcgen05.mma costs ~100-150 cycles to issue into a
-// dependent accumulator, whatever its N), so its loop is kept minimal: two
-// barrier waits, four or eight MMAs with precomputed descriptors, one commit.  The token tiles
+// Warp roles (512 threads): 0 token-tile TMA producer, 1 MMA issuer (+TMEM
+// owner), 2-5 epilogue, 6-13 dequant, 14 weight TMA producer, 15 second MMA
+// issuer.  MMA issue is on the critical path (one thread issues a tcgen05.mma
+// every ~115 cycles at N <= 128, ~160 at N = 256, whatever other threads
+// issue), so each issuer's loop is kept minimal -- one barrier wait, four MMAs
+// with precomputed descriptors, one commit -- and the 128x64 MMAs of tiles
+// above 256 token rows have their own issuer.  The token tiles
 // (4 x 40 KiB stages) and the weights (6 x 4 KiB e2m1 stages, 6 x 32 TMEM
 // columns) have separate rings so the dequant can run further ahead than the
 // large token stages allow.  Every wait is bounded (timeout -> status word +
@@ -50,7 +52,8 @@ constexpr int kACol = 320;                   constexpr int kTmemCols = 512;
 constexpr int kDeqGroups = 2;
 constexpr int kWarpTMA = 0, kWarpMMA = 1, kWarpEpi0 = 2, kWarpDeq0 = 6;
 constexpr int kWarpTMA_A = kWarpDeq0 + 4 * kDeqGroups;  // weight-ring producer
-constexpr int kThreads = (kWarpTMA_A + 1) * 32;
+constexpr int kWarpMMA2 = kWarpTMA_A + 1;              // second MMA issuer: the 128x64 MMAs of tiles above 256 rows
+constexpr int kThreads = (kWarpMMA2 + 1) * 32;
 // barriers: fullB per token stage; fullA, adone, emptyA per weight stage (emptyA
 // also frees the token stage of the same K step); sfull, sempty per scale
 // buffer; accfull, accempty, drain
@@ -211,15 +214,15 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_kernel(
     for (int s = 0; s < kStagesA; ++s) {
       ptx::mbar_init(fullA(s), 1);
       ptx::mbar_init(adone(s), 4);
-      ptx::mbar_init(emptyA(s), 1);
+      ptx::mbar_init(emptyA(s), 2);  // a commit from each MMA issuer
     }
     for (int b = 0; b < 2; ++b) {
       ptx::mbar_init(sfull(b), 1);
       ptx::mbar_init(sempty(b), 4 * kDeqGroups);
     }
-    ptx::mbar_init(accfull, 1);
+    ptx::mbar_init(accfull, 2);
     ptx::mbar_init(accempty, 4);
-    ptx::mbar_init(drain, 1);
+    ptx::mbar_init(drain, 2);
     *abort_flag = 0;
     ptx::fence_mbar_init();
   }
@@ -308,9 +311,15 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_kernel(
       }
     }
     __syncwarp();
-  } else if (warp == kWarpMMA) {
-    // ------------------------------------------------------------ MMA issuer
+  } else if (warp == kWarpMMA || warp == kWarpMMA2) {
+    // ------------------------------------------------------------ MMA issuers
+    // One thread issues a tcgen05.mma every ~115 cycles (N <= 128; ~160 at
+    // N = 256) whatever other threads issue, so the second accumulator of a
+    // tile above 256 rows (its 128x64 MMAs) has its own issuer: warp
+    // kWarpMMA issues the N <= 256 MMAs, warp kWarpMMA2 the rest; both wait
+    // for the same operands and both commit every stage and tile.
     if (lane == 0) {
+      const bool second = warp == kWarpMMA2;
       uint32_t g = 0, j = 0;
       bool ok = true;
       bool issued = false;
@@ -319,8 +328,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_kernel(
       for (int item = blockIdx.x; ok && item < total; item += gridDim.x, ++j) {
         const Tile t = decode_item(off, ipre, E, MT, item);
         const uint32_t n1 = t.nmma < 256 ? t.nmma : 256, n2 = t.nmma - n1;
-        const uint32_t id1 = ptx::idesc_bf16_f32(kBM, n1);
-        const uint32_t id2 = n2 ? ptx::idesc_bf16_f32(kBM, n2) : 0u;
+        const uint32_t id = second ? (n2 ? ptx::idesc_bf16_f32(kBM, n2) : 0u) : ptx::idesc_bf16_f32(kBM, n1);
+        const bool any = !second || n2 > 0;  // the second issuer has nothing to do for tiles of <= 256 rows
+        const uint32_t dacc = second ? tbase + 256 : tbase;
         if (!ptx::mbar_wait(accempty, (j & 1) ^ 1, abort_flag)) { ok = false; break; }
         ptx::tc_fence_after();
         for (int ks = 0; ks < KS; ++ks, ++g) {
@@ -331,38 +341,26 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_kernel(
             ok = false;
             break;
           }
-          ptx::tc_fence_after();
-          // descriptors advance by adding to the 16-byte start-address field
-          const uint64_t bd = bdesc0 + (uint64_t)((sb * kBBytes) >> 4);
-          const uint32_t at = a_t0 + sa * (kBK / 2);
-          const uint32_t acc0 = ks > 0 ? 1u : 0u;
-          if (n2) {
-            // two independent accumulators, issued alternately so that each
-            // MMA's dependency on its own accumulator overlaps the other's
-            const uint64_t bd2 = bd + (uint64_t)((256 * 128) >> 4);
-            ptx::mma_ts_bf16(tbase, at + 0, bd + 0, id1, acc0);
-            ptx::mma_ts_bf16(tbase + 256, at + 0, bd2 + 0, id2, acc0);
-            ptx::mma_ts_bf16(tbase, at + 8, bd + 2, id1, 1u);
-            ptx::mma_ts_bf16(tbase + 256, at + 8, bd2 + 2, id2, 1u);
-            ptx::mma_ts_bf16(tbase, at + 16, bd + 4, id1, 1u);
-            ptx::mma_ts_bf16(tbase + 256, at + 16, bd2 + 4, id2, 1u);
-            ptx::mma_ts_bf16(tbase, at + 24, bd + 6, id1, 1u);
-            ptx::mma_ts_bf16(tbase + 256, at + 24, bd2 + 6, id2, 1u);
-          } else {
-            ptx::mma_ts_bf16(tbase, at + 0, bd + 0, id1, acc0);
-            ptx::mma_ts_bf16(tbase, at + 8, bd + 2, id1, 1u);
-            ptx::mma_ts_bf16(tbase, at + 16, bd + 4, id1, 1u);
-            ptx::mma_ts_bf16(tbase, at + 24, bd + 6, id1, 1u);
+          if (any) {
+            ptx::tc_fence_after();
+            // descriptors advance by adding to the 16-byte start-address field
+            const uint64_t bd = bdesc0 + (uint64_t)((sb * kBBytes) >> 4) + (second ? (uint64_t)((256 * 128) >> 4) : 0u);
+            const uint32_t at = a_t0 + sa * (kBK / 2);
+            const uint32_t acc0 = ks > 0 ? 1u : 0u;
+            ptx::mma_ts_bf16(dacc, at + 0, bd + 0, id, acc0);
+            ptx::mma_ts_bf16(dacc, at + 8, bd + 2, id, 1u);
+            ptx::mma_ts_bf16(dacc, at + 16, bd + 4, id, 1u);
+            ptx::mma_ts_bf16(dacc, at + 24, bd + 6, id, 1u);
+            issued = true;
           }
           ptx::tc_commit(emptyA(sa));
-          issued = true;
         }
         if (!ok) break;
         ptx::tc_commit(accfull);
       }
-      if (!ok && issued) {  // every issued MMA must finish before TMEM is freed
+      if (!ok) {  // every issued MMA must finish before TMEM is freed: both issuers commit
         ptx::tc_commit(drain);
-        ptx::mbar_wait(drain, 0, abort_flag, 200000000LL);
+        if (issued) ptx::mbar_wait(drain, 0, abort_flag, 200000000LL);
       }
     }
     __syncwarp();
