@@ -55,7 +55,8 @@ constexpr int kTmemCols = 512;
 constexpr int kDeqGroups = 2;
 constexpr int kWarpTMA = 0, kWarpMMA = 1, kWarpDeq0 = 6;
 constexpr int kWarpTMA_A = kWarpDeq0 + 4 * kDeqGroups;
-constexpr int kThreads = (kWarpTMA_A + 1) * 32;
+constexpr int kWarpMMA2 = kWarpTMA_A + 1;  // second MMA issuer: the 128x64 MMAs of tiles above 256 rows
+constexpr int kThreads = (kWarpMMA2 + 1) * 32;
 // barriers: fullB per token stage; fullA, adone, emptyA per weight stage;
 // accfull, accempty, drain
 constexpr int kNumBars = kStagesB + 3 * kStagesA + 3;
@@ -194,11 +195,11 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_t_kernel(
     for (int s = 0; s < kStagesA; ++s) {
       ptx::mbar_init(fullA(s), 1);
       ptx::mbar_init(adone(s), 4);
-      ptx::mbar_init(emptyA(s), 1);
+      ptx::mbar_init(emptyA(s), 2);  // a commit from each MMA issuer
     }
-    ptx::mbar_init(accfull, 1);
+    ptx::mbar_init(accfull, 2);
     ptx::mbar_init(accempty, 4);
-    ptx::mbar_init(drain, 1);
+    ptx::mbar_init(drain, 2);
     *abort_flag = 0;
     ptx::fence_mbar_init();
   }
@@ -275,9 +276,13 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_t_kernel(
       }
     }
     __syncwarp();
-  } else if (warp == kWarpMMA) {
-    // ------------------------------------------------------------ MMA issuer (as the forward kernel)
+  } else if (warp == kWarpMMA || warp == kWarpMMA2) {
+    // ------------------------------------------------------------ MMA issuers (as the forward kernel)
+    // warp kWarpMMA issues the N <= 256 MMAs, kWarpMMA2 the 128x64 ones of
+    // tiles above 256 rows (one thread's issue rate is the limit); both wait
+    // for the same operands and commit every stage and tile.
     if (lane == 0) {
+      const bool second = warp == kWarpMMA2;
       uint32_t gi = 0, j = 0;
       bool ok = true, issued = false;
       const uint64_t bdesc0 = ptx::sdesc_kmajor_sw128(ptx::smem_addr(smem));
@@ -285,8 +290,9 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_t_kernel(
       for (int item = blockIdx.x; ok && item < total; item += gridDim.x, ++j) {
         const Tile t = decode_item(off, ipre, E, MT, item);
         const uint32_t n1 = t.nmma < 256 ? t.nmma : 256, n2 = t.nmma - n1;
-        const uint32_t id1 = ptx::idesc_bf16_f32(kBM, n1);
-        const uint32_t id2 = n2 ? ptx::idesc_bf16_f32(kBM, n2) : 0u;
+        const uint32_t id = second ? (n2 ? ptx::idesc_bf16_f32(kBM, n2) : 0u) : ptx::idesc_bf16_f32(kBM, n1);
+        const bool any = !second || n2 > 0;
+        const uint32_t dacc = second ? tbase + 256 : tbase;
         if (!ptx::mbar_wait(accempty, (j & 1) ^ 1, abort_flag)) { ok = false; break; }
         ptx::tc_fence_after();
         for (int ks = 0; ks < KS; ++ks, ++gi) {
@@ -297,35 +303,25 @@ __global__ void __launch_bounds__(kThreads, 1) tc_grouped_t_kernel(
             ok = false;
             break;
           }
-          ptx::tc_fence_after();
-          const uint64_t bd = bdesc0 + (uint64_t)((sb * kBBytes) >> 4);
-          const uint32_t at = a_t0 + sa * (kBK / 2);
-          const uint32_t acc0 = ks > 0 ? 1u : 0u;
-          if (n2) {
-            const uint64_t bd2 = bd + (uint64_t)((256 * 128) >> 4);
-            ptx::mma_ts_bf16(tbase, at + 0, bd + 0, id1, acc0);
-            ptx::mma_ts_bf16(tbase + 256, at + 0, bd2 + 0, id2, acc0);
-            ptx::mma_ts_bf16(tbase, at + 8, bd + 2, id1, 1u);
-            ptx::mma_ts_bf16(tbase + 256, at + 8, bd2 + 2, id2, 1u);
-            ptx::mma_ts_bf16(tbase, at + 16, bd + 4, id1, 1u);
-            ptx::mma_ts_bf16(tbase + 256, at + 16, bd2 + 4, id2, 1u);
-            ptx::mma_ts_bf16(tbase, at + 24, bd + 6, id1, 1u);
-            ptx::mma_ts_bf16(tbase + 256, at + 24, bd2 + 6, id2, 1u);
-          } else {
-            ptx::mma_ts_bf16(tbase, at + 0, bd + 0, id1, acc0);
-            ptx::mma_ts_bf16(tbase, at + 8, bd + 2, id1, 1u);
-            ptx::mma_ts_bf16(tbase, at + 16, bd + 4, id1, 1u);
-            ptx::mma_ts_bf16(tbase, at + 24, bd + 6, id1, 1u);
+          if (any) {
+            ptx::tc_fence_after();
+            const uint64_t bd = bdesc0 + (uint64_t)((sb * kBBytes) >> 4) + (second ? (uint64_t)((256 * 128) >> 4) : 0u);
+            const uint32_t at = a_t0 + sa * (kBK / 2);
+            const uint32_t acc0 = ks > 0 ? 1u : 0u;
+            ptx::mma_ts_bf16(dacc, at + 0, bd + 0, id, acc0);
+            ptx::mma_ts_bf16(dacc, at + 8, bd + 2, id, 1u);
+            ptx::mma_ts_bf16(dacc, at + 16, bd + 4, id, 1u);
+            ptx::mma_ts_bf16(dacc, at + 24, bd + 6, id, 1u);
+            issued = true;
           }
           ptx::tc_commit(emptyA(sa));
-          issued = true;
         }
         if (!ok) break;
         ptx::tc_commit(accfull);
       }
-      if (!ok && issued) {
+      if (!ok) {  // every issued MMA must finish before TMEM is freed: both issuers commit
         ptx::tc_commit(drain);
-        ptx::mbar_wait(drain, 0, abort_flag, 200000000LL);
+        if (issued) ptx::mbar_wait(drain, 0, abort_flag, 200000000LL);
       }
     }
     __syncwarp();
