@@ -510,20 +510,18 @@ __device__ void route_dispatch(const MxArgs& p, int* scratch, int* s_slot, int2*
   __syncthreads();
 }
 
-// MODE 0 epilogue of four tokens (chunk c) once their accumulators are read:
-// clamped SwiGLU of the (gate, up) row pairs, and h re-split into four e2m1
-// terms with their e8m0 scales for the down projection.  Rows alternate
-// gate / up: h_i (i = row / 2) sits in lanes 2m, 2m+1; a 32-block of h is 64
-// rows = warps (0,1) or (2,3); the byte of codes (h_i, h_i+1), i even, is
-// written by lane 4m'.  `dry`: the same instructions with every store
-// skipped, run once by the epilogue warps while the first stages stream, so
-// that the real pass does not fetch its instructions while HBM is saturated
-// (a few microseconds otherwise).  Out of line: one copy serves both.
-__device__ __noinline__ void h_terms(const MxArgs& p, float a0, float a1, float a2, float a3, int c, int ntok,
-                                     bool rv, int row_lo, int i, int ew, int lane, float (*red)[8][4],
-                                     bool unrolled, bool dry) {
-  const float acc[4] = {a0, a1, a2, a3};
-  float r[4];
+// MODE 0 epilogue of four tokens (chunk c) once their accumulators are read,
+// by one epilogue group (four warps, warp q holding tile rows 32 q..32 q+31):
+// clamped SwiGLU of the (gate, up) row pairs, then h re-split into four e2m1
+// terms with their e8m0 scales for the down projection.  Rows alternate gate
+// / up, so lanes 2m, 2m+1 of warp q give h index 16 q + m of the tile's 64;
+// the values go through shared memory so that each 32-value block of h (the
+// unit of an e8m0 scale) sits in one warp, which then computes the four terms
+// with shuffles alone: warp q takes (token, block) pairs q and q + 4.
+// i0: the tile's first h index; hb: the group's [4 tokens][64] buffer.
+__device__ __forceinline__ void h_terms(const MxArgs& p, const float (&acc)[4], int c, int ntok, int row_lo, int i0,
+                                        int q, int lane, float (*hb)[64], int ebar) {
+  const int I = p.Nw >> 1;
 #pragma unroll
   for (int jj = 0; jj < 4; ++jj) {
     const float other = __shfl_xor_sync(0xffffffffu, acc[jj], 1);
@@ -531,40 +529,29 @@ __device__ __noinline__ void h_terms(const MxArgs& p, float a0, float a1, float 
     // the reference's clamped SwiGLU (gptoss.py:130-135) with the hardware
     // exponential and division: a few ulp, far below the e2m1 terms' error
     const float gc = fminf(gate, p.limit), uc = fminf(fmaxf(up, -p.limit), p.limit);
-    r[jj] = (uc + 1.0f) * __fdividef(gc, 1.0f + __expf(-p.alpha * gc));
+    const float hv = (uc + 1.0f) * __fdividef(gc, 1.0f + __expf(-p.alpha * gc));
+    if (!(lane & 1)) hb[jj][16 * q + (lane >> 1)] = hv;
   }
-  const int I = p.Nw >> 1;
-  auto term_step = [&](int term) {
-#pragma unroll
-    for (int jj = 0; jj < 4; ++jj) {
-      const float m = group_max<32>(fabsf(r[jj]));
-      if (lane == 0) red[term & 1][ew][jj] = m;
-    }
-    named_sync(2 + (ew >> 1), 64);  // a 32-block of h: the group's subpartitions (0, 1) or (2, 3)
-#pragma unroll
-    for (int jj = 0; jj < 4; ++jj) {
-      const int tok = c * 4 + jj;
-      const uint32_t sb = e8m0_for_max(fmaxf(red[term & 1][ew][jj], red[term & 1][ew ^ 1][jj]));
-      const float q = r[jj] * exp2_neg(sb);
-      const float qn = __shfl_down_sync(0xffffffffu, q, 2);  // h_{i+1}
-      const uint32_t byte = ptx::e2m1x2_from_f32(q, qn);
-      r[jj] -= ptx::e2m1_lo_to_f32(byte) * exp2_pos(sb);
-      if (tok < ntok && rv && !dry) {
-        const int64_t hr = (int64_t)(row_lo + tok) * kTerms + term;
-        if ((lane & 3) == 0) p.hq[hr * (I / 2) + (i >> 1)] = (uint8_t)byte;
-        if (lane == 0 && !(ew & 1)) p.hs[hr * p.gp_out + (i >> 5)] = (uint8_t)sb;
-      }
-    }
-  };
-  // a single chunk (few tokens: its latency is exposed) loops over the
-  // terms; more chunks (throughput) run them unrolled
-  if (!unrolled) {
+  named_sync(ebar, 128);
 #pragma unroll 1
-    for (int term = 0; term < kTerms; ++term) term_step(term);
-  } else {
-#pragma unroll
-    for (int term = 0; term < kTerms; ++term) term_step(term);
+  for (int pr = q; pr < 8; pr += 4) {
+    const int jj = pr & 3, blk = pr >> 2, tok = c * 4 + jj;
+    if (tok >= ntok) continue;  // uniform over the warp
+    float r = hb[jj][32 * blk + lane];
+    const int i = i0 + 32 * blk + lane;  // h index of this lane
+#pragma unroll 1
+    for (int term = 0; term < kTerms; ++term) {
+      const uint32_t sb = e8m0_for_max(group_max<32>(fabsf(r)));
+      const float qv = r * exp2_neg(sb);
+      const float qn = __shfl_down_sync(0xffffffffu, qv, 1);  // h_{i+1}
+      const uint32_t byte = ptx::e2m1x2_from_f32(qv, qn);    // low nibble: this lane's value
+      r -= ptx::e2m1_lo_to_f32(byte) * exp2_pos(sb);
+      const int64_t hr = (int64_t)(row_lo + tok) * kTerms + term;
+      if (!(lane & 1)) p.hq[hr * (I / 2) + (i >> 1)] = (uint8_t)byte;
+      if (lane == 0) p.hs[hr * p.gp_out + (i >> 5)] = (uint8_t)sb;
+    }
   }
+  named_sync(ebar, 128);  // hb is rewritten by the next chunk
 }
 
 // MODE 0: B = the four term rows of tokens (every token's when resident or
@@ -584,7 +571,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
   __shared__ uint64_t bars[3 * kMaxStages + 2 * kMaxRing + 6 + 2 * kSfWarps];
   __shared__ uint32_t tmem_holder;
   __shared__ volatile int abort_flag;
-  __shared__ float red[2][8][4];
+  __shared__ float hbuf[2][4][64];  // MODE 0 epilogue: h of four tokens, per epilogue group
   __shared__ int2 s_grp[kMaxGroups];  // (expert | tokens << 16, first row)
   __shared__ int s_ngrp;
   __shared__ int s_slot[MODE == 0 ? kMaxDecodeT * 32 : 1];  // MODE 0: slot of each dispatch row
@@ -995,7 +982,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
     // epilogues run at once (at a few tokens one epilogue outlasts a piece's
     // MMAs).  With a single buffer group 1 has nothing to do.
     const int eg = warp >= 12 ? 1 : 0, ew = eg * 4 + (warp & 3);
-    const int ebar = eg ? 6 : 1;  // the group's named barrier (h_terms' pairs use 2-5)
+    const int ebar = eg ? 2 : 1;  // the group's named barrier
     const uint32_t lanes = (uint32_t)(32 * (warp & 3)) << 16;
     bool ok = true;
     for (int pc = eg; pc < n_pc && ok && eg < p.nacc; pc += p.nacc) {
@@ -1024,13 +1011,6 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
         const int sl = MODE == 0 ? s_slot[row_lo + lane] : p.slot_of_row[row_lo + lane];
         col = (MODE == 0 && !gather) ? kTerms * (sl / p.k) : kTerms * lane;
         if (MODE == 1) wt = p.scores[sl];
-      }
-      if (MODE == 0 && owner) {
-        // while the piece's MMAs run, the SwiGLU / term code once on made-up
-        // values (stores skipped), so that the real pass finds it cached
-        const bool ready = ptx::mbar_try_wait(accfull(ab), (pc / p.nacc) & 1);
-        if (!named_and(ebar, 128, ready))
-          h_terms(p, 0.f, 0.f, 0.f, 0.f, 0, 0, false, 0, 0, ew, lane, red, ntok > 4, true);
       }
       bool got = ptx::mbar_wait(accfull(ab), (pc / p.nacc) & 1, &abort_flag);
       for (int c2 = c_first; got && c2 < (int)blockIdx.x; ++c2)
@@ -1080,8 +1060,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
             if (tok < ntok && rv) p.y[(int64_t)(row_lo + tok) * Nw + r0 + lrow] = acc[jj] * w;
           }
         } else {
-          h_terms(p, acc[0], acc[1], acc[2], acc[3], c, ntok, rv, row_lo, (r0 + lrow) >> 1, ew, lane, red,
-                  nchunk > 1, false);
+          h_terms(p, acc, c, ntok, row_lo, r0 >> 1, warp & 3, lane, hbuf[eg], ebar);
         }
       }
       if (!owner) {
