@@ -1012,9 +1012,19 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
         col = (MODE == 0 && !gather) ? kTerms * (sl / p.k) : kTerms * lane;
         if (MODE == 1) wt = p.scores[sl];
       }
-      bool got = ptx::mbar_wait(accfull(ab), (pc / p.nacc) & 1, &abort_flag);
+      // the head pieces' partial sums (written early by the CTAs below, which
+      // process them first) of the first four tokens: loaded while this
+      // piece's MMAs finish
+      bool got = true;
+      float pre[4] = {0.f, 0.f, 0.f, 0.f};
       for (int c2 = c_first; got && c2 < (int)blockIdx.x; ++c2)
-        if (nonempty(c2)) got = wait_flag(p.flags + c2, 4u, &abort_flag);
+        if (nonempty(c2)) {
+          got = wait_flag(p.flags + c2, 4u, &abort_flag);
+          const float* pp = p.part + (int64_t)c2 * kGroupTok * kBM + lrow;
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) pre[jj] += __ldcg(pp + jj * kBM);
+        }
+      got = got && ptx::mbar_wait(accfull(ab), (pc / p.nacc) & 1, &abort_flag);
       if (!named_and(ebar, 128, got)) break;
       ptx::tc_fence_after();
       const uint32_t tl = tmem + lanes + ab * nb;     // pipeline 0's accumulator
@@ -1022,9 +1032,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
       const bool two = q.kc1 - q.kc0 >= 2;
       const int nchunk = (ntok + 3) / 4;
       for (int c = 0; c < nchunk; ++c) {
-        // the head pieces' sums of these four tokens: all loads in flight at once
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        for (int c2 = c_first; c2 < (int)blockIdx.x; ++c2)
+        // the head pieces' sums of these four tokens (the first four's are loaded)
+        float acc[4] = {c ? 0.f : pre[0], c ? 0.f : pre[1], c ? 0.f : pre[2], c ? 0.f : pre[3]};
+        for (int c2 = c_first; c > 0 && c2 < (int)blockIdx.x; ++c2)
           if (nonempty(c2)) {
             const float* pp = p.part + ((int64_t)c2 * kGroupTok + c * 4) * kBM + lrow;
 #pragma unroll
