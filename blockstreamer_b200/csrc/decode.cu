@@ -12,7 +12,7 @@
 // residual sets the next scale).  Four terms keep the dot products within
 // ~1e-4 relative of exact, far inside the layer's 5e-3 bar; the terms are
 // separate B rows (N = 4 x tokens), whose products are summed in the epilogue.
-// On this GPU an M=128 block-scaled MMA costs ~143 cycles whatever N is, so
+// At these N the cost of an M=128 block-scaled MMA does not depend on N, so
 // the instruction count -- weights / (128 x 64) -- sets the tensor-core time;
 // K = 64 per instruction keeps it under the HBM time of the weights.
 //
@@ -36,12 +36,13 @@
 // holding its last stage, which adds the others' partial sums (written to
 // the workspace, counted by a flag per CTA) before its epilogue.
 //
-// One CTA per SM, two pipelines that take alternate stages of every piece,
-// each with a TMA warp (weight tiles [128 rows x 256 codes] as stored, the B
-// term rows; pipeline 0's also the per-item scale blocks and B tiles), an MMA
-// thread, four scale-factor warps (one per 32-lane TMEM subpartition, writing
-// each stage's scale factors with tcgen05.st) and its own accumulator; warps
-// 0-3 add the two accumulators in the epilogue.  Measured on this GPU: one
+// One CTA per SM (512 threads), two pipelines that take alternate stages of
+// every piece, each with a TMA warp (weight tiles [128 rows x 256 codes] as
+// stored, the B term rows; pipeline 0's also the per-item scale blocks and B
+// tiles), an MMA thread with its own accumulator, and two scale-factor warps
+// (a stage's scales laid out in shared memory, copied into TMEM by
+// tcgen05.cp); two epilogue groups of four warps drain alternate accumulator
+// buffers, adding the two pipelines' accumulators.  Measured on this GPU: one
 // thread issues a block-scaled MMA every ~115 cycles and a commit in ~90,
 // whatever other threads of the SM issue, so the issuing threads' own
 // instructions set the stage rate; two pipelines double it.  The loops have
