@@ -796,9 +796,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
       const int trow = (gather && lane < ntok) ? (s_slot[gr.y + lane] / p.k) * kTerms : 0;
       bool w = true;
       // pipeline 0: this piece's per-item blocks, once their buffer is free
-      if (pl == 0 && !issue_items(pc)) break;
+      if (pl == 0 && n_issued <= pc && !issue_items(pc)) break;
       for (int kc = q.kc0 + pl; kc < q.kc1; kc += 2, ++g) {
         const int sl = pl * Sp + s;
+        // with three or more per-item buffers the next piece's blocks go out
+        // a piece ahead (its buffer was freed by the piece NR back, long done)
+        if (pl == 0 && NR >= 3 && kc == q.kc0 && n_issued == pc + 1 && pc + 1 < n_pc) {
+          bool fr = true;
+          if (lane == 0 && pc + 1 >= NR) fr = ptx::mbar_test(bfree((pc + 1) % NR), (((pc + 1) / NR) - 1) & 1);
+          if (__shfl_sync(full, fr, 0)) issue_items(pc + 1);
+        }
         if (lane == 0 && g >= Sp) w = ptx::mbar_wait(empty(sl), ph ^ 1, &abort_flag);
         if (!__shfl_sync(full, w, 0)) {
           ok = false;
@@ -1156,8 +1163,9 @@ int plan_mx(MxArgs& a, std::initializer_list<int> modes) {
   for (int b_mode : modes) {
     // an even count: the two pipelines hold half each
     for (int S = kMaxStages; S >= ((b_mode == kBStage || b_mode == kBGather) ? 2 : 4); S -= 2) {
-      const int nsc = 2;
-      if (mx_smem(a.K, a.nb, b_mode, a.gp, S, nsc).total <= budget) {
+      if (mx_smem(a.K, a.nb, b_mode, a.gp, S, 2).total <= budget) {
+        // a third per-item buffer (the next piece's blocks a piece ahead) if it costs no stage
+        const int nsc = mx_smem(a.K, a.nb, b_mode, a.gp, S, 3).total <= budget ? 3 : 2;
         a.b_mode = b_mode, a.stages = S, a.nsc = nsc;
         break;
       }
