@@ -748,8 +748,9 @@ __global__ void __launch_bounds__(kThreads, 1) decode_mx_kernel(const __grid_con
     bool ok = true;
     // Per-item blocks (A scale rows, B scale rows, kBItem's B tiles) of piece
     // pi, once its ring buffer is free (the MMAs of the piece NR earlier
-    // finished).  False on a timeout.  (Issuing the next piece's blocks
-    // during this piece's stages measured no faster.)
+    // finished).  False on a timeout.  With three buffers the next piece's
+    // blocks are issued at the start of this piece (with two, the buffer it
+    // needs frees only as this piece begins, which measured no faster).
     auto issue_items = [&](int pi) {
       const int b = pi % NR;
       bool fr = pi < NR;
